@@ -1,0 +1,279 @@
+// The quantized KV-cache write path.
+//
+// bpt_paged_kv_write: one warp per (K or V, sequence, KV head, new token). The warp reads the head vector,
+// quantizes it (FP8: x / scale rounded to E4M3 with saturation; INT8: an fp16 scale from the vector's absmax,
+// then codes), and stores D bytes to slot (block, offset) of the pool, plus the scale for INT8. Division is
+// IEEE (__fdiv_rn) and rounding is half-to-even, so the codes equal the CPU reference's bit for bit.
+//
+// bpt_kivi_quantize: the KIVI grids of kernels/reference.py for whole key groups. Keys: one thread per
+// (sequence, head, group, channel [pair]) over the group's tokens; values: one warp per token over its
+// head vector. 4-bit codes are packed channel d low / d + D/2 high.
+#include "common.cuh"
+
+namespace bpt {
+namespace {
+
+template <int DT>
+__device__ __forceinline__ float ld(const void* p, int64_t i) {
+  return load_as_float<DT>(p, i);
+}
+
+template <int DT, int VPL, int KIND>
+__global__ void paged_kv_write_kernel(const void* __restrict__ k, const void* __restrict__ v, int64_t sb, int64_t sh,
+                                      int64_t sq, int B, int Hkv, int Q, const int32_t* __restrict__ wblocks,
+                                      const int32_t* __restrict__ woffsets, uint8_t* __restrict__ k_pool,
+                                      uint8_t* __restrict__ v_pool, float k_scale, float v_scale,
+                                      __half* __restrict__ k_scales, __half* __restrict__ v_scales, int block_size,
+                                      int64_t num_blocks) {
+  constexpr int D = VPL * 32;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t per_tensor = (int64_t)B * Hkv * Q;
+  if (wid >= 2 * per_tensor) return;
+  pdl_wait();
+  const bool is_v = wid >= per_tensor;
+  const int64_t idx = is_v ? wid - per_tensor : wid;
+  const int q = int(idx % Q);
+  const int h = int((idx / Q) % Hkv);
+  const int b = int(idx / ((int64_t)Q * Hkv));
+  const int32_t blk = wblocks[(int64_t)b * Q + q];
+  const int32_t off = woffsets[(int64_t)b * Q + q];
+  if (blk < 0 || blk >= num_blocks || off < 0 || off >= block_size) {
+    if (lane == 0) record_error(blk < 0 || blk >= num_blocks ? kDevErrBlockIndex : kDevErrSlotIndex);
+    return;
+  }
+  const void* src = is_v ? v : k;
+  const int64_t base = (int64_t)b * sb + (int64_t)h * sh + (int64_t)q * sq;
+  // lane owns dims [lane*VPL, lane*VPL + VPL): contiguous bytes in the pool row
+  float x[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) x[j] = ld<DT>(src, base + lane * VPL + j);
+  const int64_t slot = ((int64_t)blk * block_size + off) * Hkv + h;
+  uint8_t* dst = (is_v ? v_pool : k_pool) + slot * D + lane * VPL;
+  uint8_t bytes[VPL];
+  if constexpr (KIND == BPT_KV_FP8) {
+    const float s = is_v ? v_scale : k_scale;
+#pragma unroll
+    for (int j = 0; j < VPL; j += 2) {
+      const uint16_t two = float2_to_e4m3x2(__fdiv_rn(x[j], s), __fdiv_rn(x[j + 1], s));
+      bytes[j] = uint8_t(two & 0xFF);
+      bytes[j + 1] = uint8_t(two >> 8);
+    }
+  } else {
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) amax = fmaxf(amax, fabsf(x[j]));
+    amax = warp_max(amax);
+    __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
+    if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
+    const float s = __half2float(s16);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const float c = fminf(fmaxf(rintf(__fdiv_rn(x[j], s)), -128.f), 127.f);
+      bytes[j] = uint8_t(int8_t(int(c)));
+    }
+    if (lane == 0) (is_v ? v_scales : k_scales)[slot] = s16;
+  }
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) dst[j] = bytes[j];
+}
+
+template <int DT>
+int paged_write_dt(const void* k, const void* v, int64_t sb, int64_t sh, int64_t sq, int64_t B, int64_t Hkv,
+                   int64_t Q, int64_t D, const int32_t* wb, const int32_t* wo, void* kp, void* vp, int kind, float ks,
+                   float vs, void* kss, void* vss, int64_t bs, int64_t nb, cudaStream_t stream) {
+  const int64_t warps = 2 * B * Hkv * Q;
+  const int threads = 256;
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  BPT_REQUIRE(blocks < (1ll << 31), BPT_ERR_INVALID, "paged kv write: too many tokens");
+#define BPT_KVW(VPL, KIND)                                                                                        \
+  paged_kv_write_kernel<DT, VPL, KIND><<<unsigned(blocks), threads, 0, stream>>>(                                 \
+      k, v, sb, sh, sq, int(B), int(Hkv), int(Q), wb, wo, static_cast<uint8_t*>(kp), static_cast<uint8_t*>(vp), ks, \
+      vs, static_cast<__half*>(kss), static_cast<__half*>(vss), int(bs), nb)
+  if (kind == BPT_KV_FP8) {
+    if (D == 64) BPT_KVW(2, BPT_KV_FP8);
+    else if (D == 128) BPT_KVW(4, BPT_KV_FP8);
+    else BPT_KVW(8, BPT_KV_FP8);
+  } else {
+    if (D == 64) BPT_KVW(2, BPT_KV_INT8);
+    else if (D == 128) BPT_KVW(4, BPT_KV_INT8);
+    else BPT_KVW(8, BPT_KV_INT8);
+  }
+#undef BPT_KVW
+  return check_launch("paged kv write");
+}
+
+// ---- KIVI -----------------------------------------------------------------------------------------------------
+
+// Keys: per (b, h, group, channel c) over `group` tokens. With bits 4 the thread owns channels c and c + D/2.
+template <int DT>
+__global__ void kivi_keys_kernel(const void* __restrict__ k, int B, int Hkv, int T, int D, int bits, int group,
+                                 uint8_t* __restrict__ codes, __half* __restrict__ kscale, __half* __restrict__ kzero,
+                                 int64_t t_max, int64_t n_groups, int64_t t0) {
+  const int per_group = bits == 4 ? D / 2 : D;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)B * Hkv * (T / group) * per_group;
+  if (tid >= total) return;
+  const int c = int(tid % per_group);
+  const int gi = int((tid / per_group) % (T / group));
+  const int h = int((tid / ((int64_t)per_group * (T / group))) % Hkv);
+  const int b = int(tid / ((int64_t)per_group * (T / group) * Hkv));
+  const float qmax = float((1 << bits) - 1);
+  const int nch = bits == 4 ? 2 : 1;
+  uint8_t out_codes[2][64];  // at most group 64 tokens per thread
+  for (int ch = 0; ch < nch; ++ch) {
+    const int d = c + ch * (D / 2);
+    const int64_t src0 = (((int64_t)b * Hkv + h) * T + (int64_t)gi * group) * D + d;
+    float lo = 0.f, hi = 0.f;
+    for (int t = 0; t < group; ++t) {
+      const float x = load_as_float<DT>(k, src0 + (int64_t)t * D);
+      lo = fminf(lo, x);
+      hi = fmaxf(hi, x);
+    }
+    __half s16 = __float2half_rn(__fdiv_rn(hi - lo, qmax));
+    if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
+    const float s = __half2float(s16);
+    const float z = fminf(fmaxf(rintf(__fdiv_rn(-lo, s)), 0.f), qmax);
+    const int64_t g_out = ((int64_t)b * Hkv + h) * n_groups + (t0 / group) + gi;
+    kscale[g_out * D + d] = s16;
+    kzero[g_out * D + d] = __float2half_rn(z);
+    for (int t = 0; t < group; ++t) {
+      const float x = load_as_float<DT>(k, src0 + (int64_t)t * D);
+      out_codes[ch][t] = uint8_t(fminf(fmaxf(rintf(__fdiv_rn(x, s)) + z, 0.f), qmax));
+    }
+  }
+  const int row_bytes = bits == 4 ? D / 2 : D;
+  for (int t = 0; t < group; ++t) {
+    const int64_t tok = t0 + (int64_t)gi * group + t;
+    const uint8_t byte = bits == 4 ? uint8_t(out_codes[0][t] | (out_codes[1][t] << 4)) : out_codes[0][t];
+    codes[(((int64_t)b * Hkv + h) * t_max + tok) * row_bytes + c] = byte;
+  }
+}
+
+// Values: one warp per (b, h, token) over the head vector.
+template <int DT>
+__global__ void kivi_values_kernel(const void* __restrict__ v, int B, int Hkv, int T, int D, int bits,
+                                   uint8_t* __restrict__ codes, __half* __restrict__ vscale, __half* __restrict__ vzero,
+                                   int64_t t_max, int64_t t0) {
+  __shared__ uint8_t stage[8][256];
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int64_t total = (int64_t)B * Hkv * T;
+  if (wid >= total) return;  // whole warps exit together (blockDim a multiple of 32)
+  const int t = int(wid % T);
+  const int64_t bh = wid / T;
+  const int64_t src0 = (bh * T + t) * D;
+  float lo = 0.f, hi = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float x = load_as_float<DT>(v, src0 + d);
+    lo = fminf(lo, x);
+    hi = fmaxf(hi, x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  const float qmax = float((1 << bits) - 1);
+  __half s16 = __float2half_rn(__fdiv_rn(hi - lo, qmax));
+  if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
+  const float s = __half2float(s16);
+  const float z = fminf(fmaxf(rintf(__fdiv_rn(-lo, s)), 0.f), qmax);
+  for (int d = lane; d < D; d += 32) {
+    const float x = load_as_float<DT>(v, src0 + d);
+    stage[wl][d] = uint8_t(fminf(fmaxf(rintf(__fdiv_rn(x, s)) + z, 0.f), qmax));
+  }
+  __syncwarp();
+  const int64_t tok = t0 + t;
+  const int row_bytes = bits == 4 ? D / 2 : D;
+  uint8_t* dst = codes + (bh * t_max + tok) * row_bytes;
+  for (int j = lane; j < row_bytes; j += 32)
+    dst[j] = bits == 4 ? uint8_t(stage[wl][j] | (stage[wl][j + D / 2] << 4)) : stage[wl][j];
+  if (lane == 0) {
+    vscale[bh * t_max + tok] = s16;
+    vzero[bh * t_max + tok] = __float2half_rn(z);
+  }
+}
+
+template <int DT>
+int kivi_quantize_dt(const void* k, const void* v, int64_t B, int64_t Hkv, int64_t T, int64_t D, int bits,
+                     int64_t group, void* kc, void* vc, void* ks, void* kz, void* vs, void* vz, int64_t t_max,
+                     int64_t n_groups, int64_t t0, cudaStream_t stream) {
+  const int per_group = bits == 4 ? int(D / 2) : int(D);
+  const int64_t kthreads = B * Hkv * (T / group) * per_group;
+  if (kthreads > 0)
+    kivi_keys_kernel<DT><<<unsigned((kthreads + 127) / 128), 128, 0, stream>>>(
+        k, int(B), int(Hkv), int(T), int(D), bits, int(group), static_cast<uint8_t*>(kc), static_cast<__half*>(ks),
+        static_cast<__half*>(kz), t_max, n_groups, t0);
+  const int64_t vwarps = B * Hkv * T;
+  if (vwarps > 0)
+    kivi_values_kernel<DT><<<unsigned((vwarps * 32 + 255) / 256), 256, 0, stream>>>(
+        v, int(B), int(Hkv), int(T), int(D), bits, static_cast<uint8_t*>(vc), static_cast<__half*>(vs),
+        static_cast<__half*>(vz), t_max, t0);
+  return check_launch("kivi quantize");
+}
+
+}  // namespace
+}  // namespace bpt
+
+using namespace bpt;
+
+extern "C" int bpt_paged_kv_write(const void* k, const void* v, int in_dtype, int64_t stride_b, int64_t stride_h,
+                                  int64_t stride_q, int64_t B, int64_t Hkv, int64_t Q, int64_t D,
+                                  const int32_t* write_blocks, const int32_t* write_offsets, void* k_pool, void* v_pool,
+                                  int kind, float k_scale_f32, float v_scale_f32, void* k_scales, void* v_scales,
+                                  int64_t block_size, int64_t num_blocks, void* stream) {
+  BPT_REQUIRE(k && v && write_blocks && write_offsets && k_pool && v_pool, BPT_ERR_INVALID,
+              "paged kv write: null pointer");
+  BPT_REQUIRE(kind == BPT_KV_FP8 || (kind == BPT_KV_INT8 && k_scales && v_scales), BPT_ERR_INVALID,
+              "paged kv write: kind %d (INT8 needs scale pools)", kind);
+  BPT_REQUIRE(D == 64 || D == 128 || D == 256, BPT_ERR_UNSUPPORTED, "paged kv write: D=%lld", (long long)D);
+  BPT_REQUIRE(B >= 0 && Hkv >= 1 && Q >= 0 && block_size >= 1 && num_blocks >= 1, BPT_ERR_INVALID,
+              "paged kv write: bad shape");
+  BPT_REQUIRE(kind != BPT_KV_FP8 || (k_scale_f32 > 0.f && v_scale_f32 > 0.f), BPT_ERR_INVALID,
+              "paged kv write: FP8 scales must be positive");
+  if (B == 0 || Q == 0) return BPT_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  switch (in_dtype) {
+    case BPT_DTYPE_F32:
+      return paged_write_dt<BPT_DTYPE_F32>(k, v, stride_b, stride_h, stride_q, B, Hkv, Q, D, write_blocks, write_offsets,
+                                           k_pool, v_pool, kind, k_scale_f32, v_scale_f32, k_scales, v_scales,
+                                           block_size, num_blocks, s);
+    case BPT_DTYPE_F16:
+      return paged_write_dt<BPT_DTYPE_F16>(k, v, stride_b, stride_h, stride_q, B, Hkv, Q, D, write_blocks, write_offsets,
+                                           k_pool, v_pool, kind, k_scale_f32, v_scale_f32, k_scales, v_scales,
+                                           block_size, num_blocks, s);
+    case BPT_DTYPE_BF16:
+      return paged_write_dt<BPT_DTYPE_BF16>(k, v, stride_b, stride_h, stride_q, B, Hkv, Q, D, write_blocks,
+                                            write_offsets, k_pool, v_pool, kind, k_scale_f32, v_scale_f32, k_scales,
+                                            v_scales, block_size, num_blocks, s);
+  }
+  return set_error(BPT_ERR_INVALID, "paged kv write: dtype %d", in_dtype);
+}
+
+extern "C" int bpt_kivi_quantize(const void* k, const void* v, int in_dtype, int64_t B, int64_t Hkv, int64_t T,
+                                 int64_t D, int bits, int64_t group, void* k_codes, void* v_codes, void* k_scale,
+                                 void* k_zero, void* v_scale, void* v_zero, int64_t t_max, int64_t n_groups, int64_t t0,
+                                 void* stream) {
+  BPT_REQUIRE(k && v && k_codes && v_codes && k_scale && k_zero && v_scale && v_zero, BPT_ERR_INVALID,
+              "kivi quantize: null pointer");
+  BPT_REQUIRE(bits == 4 || bits == 8, BPT_ERR_INVALID, "kivi quantize: bits %d (4 or 8)", bits);
+  BPT_REQUIRE(group >= 1 && group <= 64 && T % group == 0 && t0 % group == 0, BPT_ERR_INVALID,
+              "kivi quantize: T=%lld and t0=%lld must be whole groups of %lld (group <= 64)", (long long)T,
+              (long long)t0, (long long)group);
+  BPT_REQUIRE(D >= 2 && D <= 256 && D % 2 == 0, BPT_ERR_UNSUPPORTED, "kivi quantize: D=%lld", (long long)D);
+  BPT_REQUIRE(t0 + T <= t_max && (t0 + T) / group <= n_groups, BPT_ERR_INVALID, "kivi quantize: writes past the cache");
+  auto s = static_cast<cudaStream_t>(stream);
+  switch (in_dtype) {
+    case BPT_DTYPE_F32:
+      return kivi_quantize_dt<BPT_DTYPE_F32>(k, v, B, Hkv, T, D, bits, group, k_codes, v_codes, k_scale, k_zero, v_scale,
+                                             v_zero, t_max, n_groups, t0, s);
+    case BPT_DTYPE_F16:
+      return kivi_quantize_dt<BPT_DTYPE_F16>(k, v, B, Hkv, T, D, bits, group, k_codes, v_codes, k_scale, k_zero, v_scale,
+                                             v_zero, t_max, n_groups, t0, s);
+    case BPT_DTYPE_BF16:
+      return kivi_quantize_dt<BPT_DTYPE_BF16>(k, v, B, Hkv, T, D, bits, group, k_codes, v_codes, k_scale, k_zero,
+                                              v_scale, v_zero, t_max, n_groups, t0, s);
+  }
+  return set_error(BPT_ERR_INVALID, "kivi quantize: dtype %d", in_dtype);
+}

@@ -1,0 +1,129 @@
+"""W4A16 kernels against the CPU oracle (oracle/w4a16.py): codes bit-exact, bf16 outputs within
+atol 1e-2 / rtol 1e-2 of the fp32 dequantize-then-matmul reference (the tolerance of the north star)."""
+
+import pytest
+import torch
+
+from oracle import w4a16 as ow4
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"atol": 1e-2, "rtol": 1e-2}
+
+
+def dense(n, k, seed=0, std=0.02):
+    return torch.randn(n, k, generator=torch.Generator().manual_seed(seed)) * std
+
+
+def acts(m, k, seed=1):
+    return torch.randn(m, k, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("n,k,group", [(6144, 2048, 128), (96, 256, 128), (64, 6144, 128), (40, 512, 64), (24, 96, 32)])
+def test_quantize_is_bit_exact(n, k, group):
+    from bpt_b200.kernels.w4a16 import quantize_w4a16
+
+    w = dense(n, k, seed=n)
+    w[0, :group] = 0.0  # an all-zero group
+    w[1, group:] = w[1, group:].abs() + 0.01 if k > group else w[1, group:]
+    for src in (w, w.to(torch.bfloat16)):
+        qweight, scales, qzeros = quantize_w4a16(src.cuda(), group)
+        codes, s, z = ow4.quantize_w4a16(src.float(), group)
+        want_q, want_s, want_z = ow4.pack_w4a16(codes, s, z)
+        assert torch.equal(qweight.cpu(), want_q)
+        assert torch.equal(scales.cpu(), want_s)
+        assert torch.equal(qzeros.cpu(), want_z)
+        assert torch.equal(ow4.unpack_nibbles_int32(qweight.cpu(), k), codes)  # the unpacked codes, bit for bit
+
+
+def check_linear(m, n, k, group, seed=0, symmetric=False):
+    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_linear
+
+    w = dense(n, k, seed)
+    x = acts(m, k, seed + 1)
+    qweight, scales, qzeros = quantize_w4a16(w.cuda(), group)
+    if symmetric:
+        qzeros = None
+    got = w4a16_linear(x.cuda(), qweight, scales, qzeros, group=group)
+    want = ow4.w4a16_linear(x, qweight.cpu(), scales.cpu(), None if qzeros is None else qzeros.cpu(), group)
+    assert got.dtype == torch.bfloat16 and got.shape == (m, n)
+    torch.testing.assert_close(got.cpu().float(), want.float(), **TOL)
+    # and much tighter than the tolerance against an fp64 evaluation of the same quantized weight
+    codes = ow4.unpack_nibbles_int32(qweight.cpu(), k)
+    zeros = None if qzeros is None else ow4.unpack_nibbles_int32(qzeros.cpu(), k // group)
+    exact = x.double() @ ow4.dequantize_w4a16(codes, scales.cpu(), zeros, group).double().T
+    err = (got.cpu().double() - exact).abs().max().item()
+    assert err <= 2 ** -8 * exact.abs().max().item() + 1e-6
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 16])
+def test_linear_config1_shape(m):
+    check_linear(m, 6144, 2048, 128, seed=m)
+
+
+@pytest.mark.parametrize("n,k,group", [(2048, 6144, 128), (1024, 2048, 128), (12288, 2048, 128), (1000, 512, 64),
+                                       (7, 96, 32), (130, 1024, 128), (33, 3072, 128)])
+def test_linear_shapes(n, k, group):
+    check_linear(1, n, k, group, seed=n)
+    check_linear(4, n, k, group, seed=n + 1)
+
+
+def test_symmetric_layout_without_zero_points():
+    check_linear(1, 512, 1024, 128, symmetric=True)
+
+
+def test_config1_full_size():
+    from bpt_b200 import workloads
+
+    case = workloads.config1(keep_dense=True)
+    from bpt_b200.kernels.w4a16 import w4a16_linear
+
+    got = w4a16_linear(case.x, case.qweight, case.scales, case.qzeros, group=128)
+    want = ow4.w4a16_linear(case.x.cpu(), case.qweight.cpu(), case.scales.cpu(), case.qzeros.cpu(), 128)
+    torch.testing.assert_close(got.cpu().float(), want.float(), **TOL)
+    assert case.bytes == 6_553_600
+
+
+def test_gate_up_silu_matches_two_linears():
+    from bpt_b200.kernels.w4a16 import interleave_rows, quantize_w4a16, w4a16_gate_up_silu
+
+    i, k = 6144, 2048
+    gate, up = dense(i, k, 3), dense(i, k, 4)
+    for m in (1, 3, 4):
+        x = acts(m, k, 5 + m)
+        qg, qu = quantize_w4a16(gate.cuda()), quantize_w4a16(up.cuda())
+        fused = [interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)]
+        got = w4a16_gate_up_silu(x.cuda(), *fused)
+        g = ow4.w4a16_linear(x, *[t.cpu() for t in qg], 128).float()
+        u = ow4.w4a16_linear(x, *[t.cpu() for t in qu], 128).float()
+        # the reference rounds gate and up to bf16 before silu; the fused kernel keeps fp32 throughout
+        torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
+
+
+def test_out_buffer_views_and_pdl():
+    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_linear
+
+    n, k = 512, 1024
+    qweight, scales, qzeros = quantize_w4a16(dense(n, k).cuda())
+    x = acts(6, k).cuda()
+    base = w4a16_linear(x, qweight, scales, qzeros)
+    out = torch.empty(6, n, dtype=torch.bfloat16, device="cuda")
+    again = w4a16_linear(x, qweight, scales, qzeros, out=out, pdl=True)
+    assert again.data_ptr() == out.data_ptr() and torch.equal(again, base)
+    x3 = x.reshape(2, 3, k)
+    assert torch.equal(w4a16_linear(x3, qweight, scales, qzeros).reshape(6, n), base)
+    wide = torch.zeros(6, 2 * k, dtype=torch.bfloat16, device="cuda")
+    wide[:, :k] = x
+    assert torch.equal(w4a16_linear(wide[:, :k], qweight, scales, qzeros), base)  # a strided row view
+
+
+def test_bad_arguments_raise_value_error():
+    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_linear
+
+    qweight, scales, qzeros = quantize_w4a16(dense(64, 256).cuda())
+    with pytest.raises(ValueError):
+        w4a16_linear(acts(1, 256), qweight, scales, qzeros)  # activations on the CPU
+    with pytest.raises(ValueError):
+        w4a16_linear(acts(1, 128).cuda(), qweight, scales, qzeros)  # wrong K
+    with pytest.raises(ValueError):
+        w4a16_linear(acts(1, 256).cuda(), qweight, scales, qzeros, group=64)  # scales do not match the group
