@@ -1,0 +1,436 @@
+"""Benchmark of fastserve's decode hot path on B200: W4A16 GEMV (config 1) + paged FP8-KV decode attention
+(config 2), one step = one GEMV and one attention over one batch, inputs resident in HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU; weak scaling, no collective)
+
+Prints one JSON line (rank 0). `value` is whole-job achieved HBM bandwidth: the algorithmic bytes of every
+rank's steps over the slowest rank's device time. `e2e` is the same metric through the public Python API with
+this step's inputs copied from pinned host memory and the results copied back inside the timed region.
+`--impl reference` times the reference's CPU path (the oracle port: dequantize-then-matmul and gather,
+dequantize, attend) on the host cores, on a bounded sample of the same workload.
+
+Inputs larger than L2: the GEMV rotates over 40 weight copies (262 MB) and the attention over 3 batches with
+their own pools (about 450 MB of KV touched per cycle), so no step finds its data in the 126 MB L2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT, ROOT / "bytes-per-token_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+import torch  # noqa: E402
+
+METRIC = "achieved HBM GB/s (% of B200 peak) and us/call: W4A16 GEMV + FP8-KV decode attn"
+WORKLOAD = ("config1 W4A16 GEMV (M=1, K=2048, N=6144, asym INT4 g128) + config2 paged FP8 decode attention "
+            "(B=32, 16 Q / 8 KV heads, D=128, lengths U[512,4096], page 16, 16384-page pool)")
+GEMV_COPIES = 40
+ATTN_BATCHES = 3
+PROFILE_SUMMARY = ROOT / "profiles" / "paged_attention_fp8_config2.md"
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic() -> int | None:
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary (a line
+    `traffic_bytes_per_launch: N`), scaled to this run's workload by the caller."""
+    if not PROFILE_SUMMARY.exists():
+        return None
+    for line in PROFILE_SUMMARY.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1].strip().replace(",", ""))
+    return None
+
+
+# ---- clocks -----------------------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """Samples this GPU's SM clock and throttle reasons through NVML every ~2 ms in a background thread."""
+
+    REASONS = {
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+        "sw_power_cap": 0x4,
+    }
+
+    def __init__(self, device: torch.device):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nvml = pynvml
+        except Exception as exc:  # no NVML: report no clocks rather than fail the run
+            self._nvml = None
+            self.error = repr(exc)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = statistics.median(s[0] for s in self.samples)
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        reasons = [name for name, bit in self.REASONS.items() if seen & bit]
+        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---- our arm ------------------------------------------------------------------------------------------------------
+
+
+def build_inputs(device: torch.device, seed: int):
+    from bpt_b200 import workloads
+    from bpt_b200.kernels.w4a16 import quantize_w4a16
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    weights = []
+    for _ in range(GEMV_COPIES):
+        w = torch.randn(6144, 2048, generator=g, device=device) * 0.02
+        weights.append(quantize_w4a16(w, 128))
+    x = torch.randn(1, 2048, generator=g, device=device).to(torch.bfloat16)
+    attn = [workloads.config2(device=device, seed=seed * 100 + i) for i in range(ATTN_BATCHES)]
+    return weights, x, attn
+
+
+def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
+    from bpt_b200 import workloads
+    from bpt_b200.kernels.kv_attention import attend, attend_workspace, paged_split
+    from bpt_b200.kernels.w4a16 import w4a16_linear
+
+    dist = torch.distributed if world > 1 else None
+    weights, x, attn = build_inputs(device, seed=rank)
+    scale = 1.0 / math.sqrt(128)
+    y = torch.empty(1, 6144, dtype=torch.bfloat16, device=device)
+    out = torch.empty(32, 16, 128, dtype=torch.bfloat16, device=device)
+    split = paged_split(32, 4096, 16, torch.cuda.get_device_properties(device).multi_processor_count)
+    n_splits = -(-4096 // split)
+    attend_workspace(32, 16, 128, n_splits, device)  # allocated before timing
+    gemv_bytes = workloads.w4a16_bytes(1, 6144, 2048)
+    attn_bytes = [c.bytes for c in attn]
+
+    def step(i: int, events=None):
+        qw, sc, qz = weights[i % GEMV_COPIES]
+        case = attn[i % ATTN_BATCHES]
+        if events is not None:
+            events[0].record()
+        w4a16_linear(x, qw, sc, qz, out=y)
+        if events is not None:
+            events[1].record()
+        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split)
+        if events is not None:
+            events[2].record()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    barrier()
+
+    # device-timed region: exactly K steps, events around every kernel on the launching (current) stream
+    sampler = ClockSampler(device)
+    stream = torch.cuda.current_stream(device)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with sampler:
+        soak_end = time.perf_counter() + 0.3  # the sampler needs a few hundred ms of the same load around the region
+        i = 0
+        while time.perf_counter() < soak_end:
+            step(i)
+            i += 1
+            if i % 64 == 0:
+                torch.cuda.synchronize(device)
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for k in range(args.steps):
+            step(k, ev[k])
+        end.record(stream)
+        barrier()
+    total_ms = start.elapsed_time(end)
+    gemv_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    attn_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    my_bytes = sum(gemv_bytes + attn_bytes[k % ATTN_BATCHES] for k in range(args.steps))
+
+    # end to end: the public API with host buffers, the step's inputs H2D and results D2H inside the region
+    pin = {
+        "x": torch.empty(1, 2048, dtype=torch.bfloat16).pin_memory(),
+        "q": [c.q.cpu().pin_memory() for c in attn],
+        "lengths": [c.lengths.cpu().pin_memory() for c in attn],
+        "table": [c.kv.block_table.cpu().pin_memory() for c in attn],
+        "y": torch.empty(1, 6144, dtype=torch.bfloat16).pin_memory(),
+        "out": torch.empty(32, 16, 128, dtype=torch.bfloat16).pin_memory(),
+    }
+    pin["x"].copy_(x.cpu())
+    h2d = pin["x"].numel() * 2 + pin["q"][0].numel() * 2 + pin["lengths"][0].numel() * 4 + pin["table"][0].numel() * 4
+    d2h = pin["y"].numel() * 2 + pin["out"].numel() * 2
+
+    def e2e_step(i: int):
+        case = attn[i % ATTN_BATCHES]
+        qw, sc, qz = weights[i % GEMV_COPIES]
+        x.copy_(pin["x"], non_blocking=True)
+        case.q.copy_(pin["q"][i % ATTN_BATCHES], non_blocking=True)
+        case.lengths.copy_(pin["lengths"][i % ATTN_BATCHES], non_blocking=True)
+        case.kv.block_table.copy_(pin["table"][i % ATTN_BATCHES], non_blocking=True)
+        w4a16_linear(x, qw, sc, qz, out=y)
+        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split)
+        pin["y"].copy_(y, non_blocking=True)
+        pin["out"].copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for k in range(args.steps):
+        e2e_step(k)
+    e_end.record(stream)
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    local = {
+        "total_ms": total_ms,
+        "e2e_ms": e2e_ms,
+        "bytes": my_bytes,
+        "gemv_ms": gemv_ms,
+        "attn_ms": attn_ms,
+        "clocks": sampler.summary(),
+    }
+    if dist is not None:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, local)
+    else:
+        gathered = [local]
+    if rank != 0:
+        return None
+
+    t_max = max(g["total_ms"] for g in gathered)
+    e_max = max(g["e2e_ms"] for g in gathered)
+    all_bytes = sum(g["bytes"] for g in gathered)
+    gbs = all_bytes / (t_max * 1e-3) / 1e9
+    e2e_gbs = all_bytes / (e_max * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+    attn_avg_ms = statistics.fmean(gathered[0]["attn_ms"])
+    gemv_avg_ms = statistics.fmean(gathered[0]["gemv_ms"])
+    attn_bytes_avg = statistics.fmean(attn_bytes)
+    achieved = attn_bytes_avg / (attn_avg_ms * 1e-3) / 1e9
+    traffic = profiled_traffic()
+    clocks = gathered[0]["clocks"]
+    reasons = sorted({r for g in gathered for r in g["clocks"]["reasons"]})
+    line = {
+        "metric": METRIC,
+        "value": round(gbs, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_max / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded; random INT4 weights N(0,0.02), K/V N(0,1) in E4M3, bf16 queries N(0,1))",
+        "config": {
+            "workload": WORKLOAD,
+            "per_rank": "one GEMV + one attention over a batch of 32 sequences per step",
+            "l2": f"inputs larger than L2: {GEMV_COPIES} rotating weight copies, {ATTN_BATCHES} rotating batches/pools",
+            "split": split,
+            "parallelism": f"dp{world} (independent request batches, no collective)",
+        },
+        "kernels": {
+            "w4a16_gemv": {"us_per_call": round(gemv_avg_ms * 1e3, 2),
+                           "gbs": round(gemv_bytes / (gemv_avg_ms * 1e-3) / 1e9, 1),
+                           "frac_of_peak": round(gemv_bytes / (gemv_avg_ms * 1e-3) / 1e9 / peak, 3),
+                           "bytes": gemv_bytes},
+            "paged_attention_fp8": {"us_per_call": round(attn_avg_ms * 1e3, 2), "gbs": round(achieved, 1),
+                                    "frac_of_peak": round(achieved / peak, 3), "bytes": round(attn_bytes_avg)},
+        },
+        "roofline": {
+            "kernel": "paged_attn_kernel<128, 2, FP8> (fused split merge)",
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 3),
+            "traffic": None if traffic is None else traffic,
+        },
+        "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e_max / args.steps, 5)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": reasons,
+                   "samples": clocks["samples"], "window": "0.3 s soak of the same step + the timed region"},
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(sample_seqs=4)
+    return line
+
+
+# ---- the CPU baseline: the reference path restated (oracle port) on the host cores ------------------------------
+
+
+def cpu_baseline(sample_seqs: int = 4, repeats: int = 3) -> dict:
+    """The reference's plain-PyTorch path on the host cores (the oracle port): W4A16 dequantize + fp32 linear at
+    the config-1 shape, and gather, dequantize, attend, merge for `sample_seqs` sequences of a config-2 batch.
+    Returns achieved GB/s over the same algorithmic bytes as the GPU metric."""
+    from oracle import attention as oatt
+    from oracle import kv_formats as okv
+    from oracle import w4a16 as ow4
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(6144, 2048, generator=g) * 0.02
+    codes, scales, zeros = ow4.quantize_w4a16(w, 128)
+    qweight, scales, qzeros = ow4.pack_w4a16(codes, scales, zeros)
+    x = torch.randn(1, 2048, generator=g).to(torch.bfloat16)
+    # a config-2 batch restricted to `sample_seqs` sequences, pool holding exactly their pages
+    lengths = torch.randint(512, 4097, (32,), generator=g)[:sample_seqs]
+    pages = int(((lengths + 15) // 16).sum())
+    table = torch.randperm(pages, generator=g)
+    width = int((lengths.max() + 15) // 16)
+    bt = torch.zeros(sample_seqs, width, dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(((lengths + 15) // 16).tolist()):
+        bt[i, :n] = table[pos : pos + n].to(torch.int32)
+        pos += n
+    kpool = okv.fp8_store(torch.randn(pages, 16, 8, 128, generator=g), 1 / 64)
+    vpool = okv.fp8_store(torch.randn(pages, 16, 8, 128, generator=g), 1 / 64)
+    kv = okv.PagedKV("fp8", kpool, vpool, 1 / 64, 1 / 64, bt, 16)
+    q = torch.randn(sample_seqs, 16, 128, generator=g).to(torch.bfloat16)
+    from bpt_b200.workloads import paged_bytes, w4a16_bytes
+
+    nbytes = w4a16_bytes(1, 6144, 2048) + paged_bytes(lengths, 16, 8, 128, "fp8")
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        ow4.w4a16_linear(x, qweight, scales, qzeros, 128)
+        oatt.paged_attend(q, kv, lengths, 1 / math.sqrt(128))
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {
+        "value": round(nbytes / t / 1e9, 3),
+        "unit": "GB/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"config-1 GEMV (full) + config-2 attention over {sample_seqs} of 32 sequences "
+                  f"({int(lengths.sum())} tokens); median of {repeats}",
+        "s_per_sample": round(t, 4),
+    }
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    for _ in range(max(args.warmup, 1)):
+        cpu_baseline(sample_seqs=4, repeats=1)
+    samples = [cpu_baseline(sample_seqs=4, repeats=1) for _ in range(args.steps)]
+    value = statistics.median(s["value"] for s in samples)
+    cores = samples[0]["cores"]
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(statistics.median(s["s_per_sample"] for s in samples) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "impl": "reference",
+        "config": {"workload": WORKLOAD, "sample": samples[0]["sample"]},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": samples[0]["sample"]},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}; using WORLD_SIZE", file=sys.stderr)
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    from datetime import timedelta
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    try:
+        line = run_ours(args, rank, world, device)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

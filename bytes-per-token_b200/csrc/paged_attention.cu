@@ -504,10 +504,16 @@ int paged_dispatch(const PagedArgs& a, int kind, int64_t D, int flags, cudaStrea
 
 }  // namespace
 
+// Workspace layout: [ticket counters: kMaxSeqs x u32][lse: B x S x Hq f32][outs: B x S x Hq x D f32].
+// The counters sit at a fixed offset whatever B and S are, so the zeros every call leaves behind are found by
+// the next call even when its shape differs.
+constexpr int64_t kMaxSeqs = 65536;
+constexpr int64_t kCounterBytes = kMaxSeqs * 4;
+
 int64_t paged_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits) {
   const int64_t outs = B * n_splits * Hq * D * 4;
   const int64_t lses = B * n_splits * Hq * 4;
-  return ((outs + 255) / 256) * 256 + ((lses + 255) / 256) * 256 + ((B * 4 + 255) / 256) * 256;
+  return kCounterBytes + ((lses + 255) / 256) * 256 + ((outs + 255) / 256) * 256;
 }
 
 }  // namespace bpt
@@ -556,13 +562,12 @@ extern "C" int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, 
               "paged attend: workspace of %lld bytes, need %lld", (long long)workspace_bytes, (long long)need);
   BPT_REQUIRE(aligned16(workspace), BPT_ERR_ALIGNMENT, "paged attend: workspace must be 16-byte aligned");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const int64_t outs = ((B * n_splits * Hq * D * 4 + 255) / 256) * 256;
   const int64_t lses = ((B * n_splits * Hq * 4 + 255) / 256) * 256;
   a.merge = 1;
   a.out = out;
   a.out_dtype = out_dtype;
-  a.ws_out = reinterpret_cast<float*>(ws);
-  a.ws_lse = reinterpret_cast<float*>(ws + outs);
-  a.ws_count = reinterpret_cast<unsigned int*>(ws + outs + lses);
+  a.ws_count = reinterpret_cast<unsigned int*>(ws);
+  a.ws_lse = reinterpret_cast<float*>(ws + kCounterBytes);
+  a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
   return paged_dispatch(a, kind, D, flags, static_cast<cudaStream_t>(stream));
 }

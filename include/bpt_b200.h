@@ -114,7 +114,8 @@ int bpt_paged_decode_partials(const void* q, int q_dtype, int64_t q_stride_b, in
 /* The merged attention out [B, Hq, D] in out_dtype, splits merged inside the same launch: the last CTA of a
  * sequence to finish combines its splits (an atomic ticket per sequence; nothing waits). `workspace` is
  * caller-owned device memory of at least bpt_paged_attend_workspace_bytes(...) bytes, ZEROED before its
- * first use; each call leaves its counters at zero again. Calls that share a workspace must not overlap.
+ * first use; its first 256 KiB hold the per-sequence tickets (B <= 65536), which every call leaves at zero
+ * again, so one workspace serves calls of any shape. Calls that share a workspace must not overlap.
  * Replaces: kernels/kv_attention.py:248-252 (attend = merge_partials(decode_attention(...))) and
  * kernels/reference.py:205-211 (merge_partials). */
 int64_t bpt_paged_attend_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits);
