@@ -36,6 +36,8 @@ SIGNATURES: dict[str, list] = {
     "bpt_paged_attend_workspace_bytes": [I64, I64, I64, I64],
     "bpt_paged_attend": [P, I32, I64, I64, P, P, I32, F32, F32, P, P, P, I64, P, I64, I64, I64, I64, I64, I64, I64, I64,
                          F32, P, I32, P, I64, I32, P],
+    "bpt_paged_attend_noalloc": [P, I32, I64, I64, P, P, I32, F32, F32, P, P, P, I64, P, I64, I64, I64, I64, I64, I64,
+                                 I64, I64, F32, P, I32, I32, P],
     "bpt_merge_partials": [P, P, I64, I64, I64, I64, P, I32, P],
     "bpt_kivi_decode_partials": [P, I32, I64, I64, I32, I32, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64,
                                  I64, I64, F32, P, P, P],

@@ -571,3 +571,82 @@ extern "C" int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, 
   a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
   return paged_dispatch(a, kind, D, flags, static_cast<cudaStream_t>(stream));
 }
+
+// ---- the no-allocation variant of bpt_paged_attend ------------------------------------------------------------
+// For callers that cannot allocate device memory: the workspace is a fixed file-scope device array instead of a
+// caller buffer. The array's name is a host-side stand-in in host code, so its device address is looked up
+// once per device (cudaGetSymbolAddress, with that device current) and passed to the kernel like any workspace.
+
+#include <mutex>
+
+namespace bpt {
+namespace {
+
+constexpr int64_t kNoAllocBytes = BPT_NOALLOC_SCRATCH_BYTES;
+static_assert(kNoAllocBytes > kCounterBytes, "the scratch must hold the ticket counters");
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+int noalloc_scratch(void** addr) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(BPT_ERR_CUDA, "paged attend (no alloc): no current device: %s", cudaGetErrorString(err));
+  BPT_REQUIRE(dev >= 0 && dev < kMaxDevices, BPT_ERR_UNSUPPORTED, "paged attend (no alloc): device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr)
+      return set_error(BPT_ERR_CUDA, "paged attend (no alloc): cannot find the scratch array on device %d: %s", dev,
+                       cudaGetErrorString(err));
+    g_noalloc_addr[dev] = p;
+  }
+  *addr = g_noalloc_addr[dev];
+  return BPT_OK;
+}
+
+}  // namespace
+}  // namespace bpt
+
+extern "C" int bpt_paged_attend_noalloc(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                        const void* k_pool, const void* v_pool, int kind, float k_scale_f32,
+                                        float v_scale_f32, const void* k_scales, const void* v_scales,
+                                        const int32_t* block_table, int64_t bt_stride, const int32_t* lengths,
+                                        int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t block_size,
+                                        int64_t num_blocks, int64_t split, int64_t n_splits, float sm_scale, void* out,
+                                        int out_dtype, int flags, void* stream) {
+  PagedArgs a;
+  int st = paged_common(a, q, q_dtype, q_stride_b, q_stride_h, k_pool, v_pool, kind, k_scale_f32, v_scale_f32,
+                        k_scales, v_scales, block_table, bt_stride, lengths, B, Hq, Hkv, D, block_size, num_blocks,
+                        split, n_splits, sm_scale);
+  if (st) return st;
+  BPT_REQUIRE(out, BPT_ERR_INVALID, "paged attend (no alloc): null output");
+  BPT_REQUIRE(out_dtype == BPT_DTYPE_F32 || out_dtype == BPT_DTYPE_F16 || out_dtype == BPT_DTYPE_BF16,
+              BPT_ERR_INVALID, "paged attend (no alloc): out dtype %d", out_dtype);
+  const int64_t need = paged_workspace_bytes(B, Hq, D, n_splits);
+  BPT_REQUIRE(need <= kNoAllocBytes, BPT_ERR_WORKSPACE,
+              "paged attend (no alloc): B=%lld x n_splits=%lld x Hq=%lld x D=%lld needs %lld bytes of scratch, above the "
+              "fixed %lld (use larger splits, or bpt_paged_attend with a caller workspace)",
+              (long long)B, (long long)n_splits, (long long)Hq, (long long)D, (long long)need, (long long)kNoAllocBytes);
+  void* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  // The array keeps whatever the last call left: the tickets this call uses must start at zero.
+  cudaError_t err = cudaMemsetAsync(scratch, 0, size_t(B) * sizeof(unsigned int), s);
+  if (err != cudaSuccess)
+    return set_error(BPT_ERR_CUDA, "paged attend (no alloc): clearing the tickets: %s", cudaGetErrorString(err));
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  const int64_t lses = ((B * n_splits * Hq * 4 + 255) / 256) * 256;
+  a.merge = 1;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.ws_count = reinterpret_cast<unsigned int*>(ws);
+  a.ws_lse = reinterpret_cast<float*>(ws + kCounterBytes);
+  a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
+  return paged_dispatch(a, kind, D, flags, s);
+}

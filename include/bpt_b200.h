@@ -126,6 +126,27 @@ int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_s
                      int64_t split, int64_t n_splits, float sm_scale, void* out, int out_dtype, void* workspace,
                      int64_t workspace_bytes, int flags, void* stream);
 
+/* bpt_paged_attend without a workspace argument, for callers that cannot allocate device memory: serving
+ * engines that hand all free HBM to their paged KV pool at start-up (so a later cudaMalloc fails or fragments
+ * the pool), runtimes whose memory policy forbids device allocation after initialization, and foreign-language
+ * hosts that only hold the buffers they were given and have no allocator to call. No counterpart in the
+ * reference (its attention allocates its partial outputs with torch.empty on every call).
+ * The split partials and tickets live in one fixed array of BPT_NOALLOC_SCRATCH_BYTES bytes, a static device
+ * variable of this library: every GPU that loads the library holds it until the process exits. A call needs
+ * 256 KiB + B * n_splits * Hq * (D + 1) * 4 bytes of it (rounded up to 256 B per part) and returns
+ * BPT_ERR_WORKSPACE, launching nothing, when that is more. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that first call before any stream
+ * capture. Each call clears the tickets it uses (an asynchronous memset on `stream`) before the kernel.
+ * All calls on a device share the array: calls that overlap on the GPU (concurrent streams) race and corrupt
+ * each other's results. Nothing here calls cudaMalloc, cudaFree or any allocating routine. */
+#define BPT_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+int bpt_paged_attend_noalloc(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_stride_h, const void* k_pool,
+                             const void* v_pool, int kind, float k_scale_f32, float v_scale_f32, const void* k_scales,
+                             const void* v_scales, const int32_t* block_table, int64_t bt_stride,
+                             const int32_t* lengths, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t block_size,
+                             int64_t num_blocks, int64_t split, int64_t n_splits, float sm_scale, void* out,
+                             int out_dtype, int flags, void* stream);
+
 /* merged[B, Hq, D] (out_dtype) = sum_s softmax_s(lse[b, h, :]) * outs[b, h, s, :]; all -inf rows give 0.
  * Replaces: kernels/reference.py:205-211 (merge_partials). */
 int bpt_merge_partials(const float* outs, const float* lses, int64_t B, int64_t Hq, int64_t S, int64_t D,
