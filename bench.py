@@ -296,7 +296,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
                                     "frac_of_peak": round(achieved / peak, 3), "bytes": round(attn_bytes_avg)},
         },
         "roofline": {
-            "kernel": "paged_attn_kernel<128, 2, FP8> (fused split merge)",
+            "kernel": "paged_attn_mma_kernel<128, 2, FP8> (fused split merge)",
             "bound": "hbm",
             "achieved": round(achieved, 1),
             "peak": peak,

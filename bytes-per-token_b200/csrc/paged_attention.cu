@@ -19,6 +19,9 @@
 // reference.merge_partials) and resets the counter. No CTA ever waits on another.
 #include <math_constants.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace bpt {
@@ -58,6 +61,9 @@ struct PagedArgs {
   int page_bytes;   // kBS * Hkv * D
   int scale_bytes;  // kBS * Hkv * 2 (INT8) or 0
   int nst;          // pipeline stages
+  // persistent kernel
+  int persist_ctas;   // CTAs (one per SM)
+  int max_cta_pages;  // capacity of a CTA's page list
 };
 
 __device__ __forceinline__ float q_load(const void* q, int dt, int64_t i) {
@@ -438,6 +444,9 @@ int launch_d(const PagedArgs& a, int D, int rep, int flags, cudaStream_t stream)
   return set_error(BPT_ERR_UNSUPPORTED, "paged attention: D=%d not in {64, 128, 256}", D);
 }
 
+#include "paged_attention_mma.cuh"
+#include "paged_attention_persistent.cuh"
+
 int paged_common(PagedArgs& a, const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, const void* k_pool,
                  const void* v_pool, int kind, float k_scale, float v_scale, const void* k_scales,
                  const void* v_scales, const int32_t* block_table, int64_t bt_stride, const int32_t* lengths,
@@ -493,27 +502,94 @@ int paged_common(PagedArgs& a, const void* q, int q_dtype, int64_t q_sb, int64_t
   a.ws_out = nullptr;
   a.ws_lse = nullptr;
   a.ws_count = nullptr;
+  a.persist_ctas = 0;
+  a.max_cta_pages = 0;
   return BPT_OK;
+}
+
+// The tensor-core kernel serves head dims 64 and 128 with up to 8 KV heads; the scalar kernel the rest.
+// BPT_PAGED_SCALAR=1 in the environment selects the scalar kernel everywhere (for comparisons).
+bool use_scalar_kernel() {
+  static const int forced = [] {
+    const char* v = getenv("BPT_PAGED_SCALAR");
+    return (v && v[0] == '1') ? 1 : 0;
+  }();
+  return forced != 0;
 }
 
 int paged_dispatch(const PagedArgs& a, int kind, int64_t D, int flags, cudaStream_t stream) {
   const int rep = a.Hq / a.Hkv;
+  if (!use_scalar_kernel() && (D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv) {
+    if (kind == BPT_KV_FP8)
+      return D == 64 ? launch_mma_rep<64, BPT_KV_FP8>(a, rep, flags, stream)
+                     : launch_mma_rep<128, BPT_KV_FP8>(a, rep, flags, stream);
+    return D == 64 ? launch_mma_rep<64, BPT_KV_INT8>(a, rep, flags, stream)
+                   : launch_mma_rep<128, BPT_KV_INT8>(a, rep, flags, stream);
+  }
   if (kind == BPT_KV_FP8) return launch_d<BPT_KV_FP8>(a, int(D), rep, flags, stream);
   return launch_d<BPT_KV_INT8>(a, int(D), rep, flags, stream);
 }
 
-}  // namespace
-
-// Workspace layout: [ticket counters: kMaxSeqs x u32][lse: B x S x Hq f32][outs: B x S x Hq x D f32].
-// The counters sit at a fixed offset whatever B and S are, so the zeros every call leaves behind are found by
-// the next call even when its shape differs.
+// Workspace layouts. Both start with the ticket counters (kMaxSeqs x u32) at a fixed offset, so the zeros every
+// call leaves behind are found by the next call whatever its shape or kernel.
+//   split kernels:      [counters][lse: B x S x Hq f32][outs: B x S x Hq x D f32]
+//   persistent kernel:  [counters][lse: (B + CTAs) x Hq f32][outs: (B + CTAs) x Hq x D f32]
 constexpr int64_t kMaxSeqs = 65536;
 constexpr int64_t kCounterBytes = kMaxSeqs * 4;
+static_assert(kCounterBytes == kCounterBytesP, "one counter region for every merge kernel");
 
-int64_t paged_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits) {
+int64_t split_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits) {
   const int64_t outs = B * n_splits * Hq * D * 4;
   const int64_t lses = B * n_splits * Hq * 4;
   return kCounterBytes + ((lses + 255) / 256) * 256 + ((outs + 255) / 256) * 256;
+}
+
+bool persistent_applies(const PagedArgs& a, int64_t D, int64_t& cap) {
+  const int G = num_sms();
+  cap = (int64_t(a.B) * a.bt_stride + G - 1) / G;
+  static const int enabled = env_int("BPT_PAGED_PERSIST", 1);
+  return enabled && !use_scalar_kernel() && (D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv &&
+         a.B <= kPersistMaxSeqs && cap <= kPersistMaxCtaPages && a.q_sh == D && a.q_sb == a.Hq * D &&
+         aligned16(a.q);
+}
+
+// The fused-merge launch: the persistent kernel where it applies, the split kernels otherwise; `ws` is the
+// workspace (caller's or the no-allocation array) of `ws_bytes` bytes.
+int merge_launch(PagedArgs& a, int kind, int64_t D, int flags, cudaStream_t stream, uint8_t* ws, int64_t ws_bytes,
+                 const char* who) {
+  const int64_t B = a.B, Hq = a.Hq;
+  int64_t cap = 0;
+  a.merge = 1;
+  if (persistent_applies(a, D, cap)) {
+    const int G = num_sms();
+    const int64_t need = persist_workspace_bytes(B, Hq, D, G);
+    BPT_REQUIRE(ws_bytes >= need, BPT_ERR_WORKSPACE, "%s: workspace of %lld bytes, need %lld", who, (long long)ws_bytes,
+                (long long)need);
+    const int64_t lses = (((B + G) * Hq * 4 + 255) / 256) * 256;
+    a.persist_ctas = G;
+    a.max_cta_pages = int(cap);
+    a.ws_count = reinterpret_cast<unsigned int*>(ws);
+    a.ws_lse = reinterpret_cast<float*>(ws + kCounterBytes);
+    a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
+    const int rep = a.Hq / a.Hkv;
+    if (kind == BPT_KV_FP8)
+      return D == 64 ? launch_persist<64, BPT_KV_FP8>(a, rep, flags, stream) : launch_persist<128, BPT_KV_FP8>(a, rep, flags, stream);
+    return D == 64 ? launch_persist<64, BPT_KV_INT8>(a, rep, flags, stream) : launch_persist<128, BPT_KV_INT8>(a, rep, flags, stream);
+  }
+  const int64_t need = split_workspace_bytes(B, Hq, D, a.n_splits);
+  BPT_REQUIRE(ws_bytes >= need, BPT_ERR_WORKSPACE, "%s: workspace of %lld bytes, need %lld", who, (long long)ws_bytes,
+              (long long)need);
+  const int64_t lses = ((B * a.n_splits * Hq * 4 + 255) / 256) * 256;
+  a.ws_count = reinterpret_cast<unsigned int*>(ws);
+  a.ws_lse = reinterpret_cast<float*>(ws + kCounterBytes);
+  a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
+  return paged_dispatch(a, kind, D, flags, stream);
+}
+
+}  // namespace
+
+int64_t paged_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits) {
+  return std::max(split_workspace_bytes(B, Hq, D, n_splits), persist_workspace_bytes(B, Hq, D, num_sms()));
 }
 
 }  // namespace bpt
@@ -557,19 +633,12 @@ extern "C" int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, 
   BPT_REQUIRE(out, BPT_ERR_INVALID, "paged attend: null output");
   BPT_REQUIRE(out_dtype == BPT_DTYPE_F32 || out_dtype == BPT_DTYPE_F16 || out_dtype == BPT_DTYPE_BF16,
               BPT_ERR_INVALID, "paged attend: out dtype %d", out_dtype);
-  const int64_t need = paged_workspace_bytes(B, Hq, D, n_splits);
-  BPT_REQUIRE(workspace && workspace_bytes >= need, BPT_ERR_WORKSPACE,
-              "paged attend: workspace of %lld bytes, need %lld", (long long)workspace_bytes, (long long)need);
+  BPT_REQUIRE(workspace, BPT_ERR_WORKSPACE, "paged attend: no workspace");
   BPT_REQUIRE(aligned16(workspace), BPT_ERR_ALIGNMENT, "paged attend: workspace must be 16-byte aligned");
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const int64_t lses = ((B * n_splits * Hq * 4 + 255) / 256) * 256;
-  a.merge = 1;
   a.out = out;
   a.out_dtype = out_dtype;
-  a.ws_count = reinterpret_cast<unsigned int*>(ws);
-  a.ws_lse = reinterpret_cast<float*>(ws + kCounterBytes);
-  a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
-  return paged_dispatch(a, kind, D, flags, static_cast<cudaStream_t>(stream));
+  return merge_launch(a, kind, D, flags, static_cast<cudaStream_t>(stream), static_cast<uint8_t*>(workspace),
+                      workspace_bytes, "paged attend");
 }
 
 // ---- the no-allocation variant of bpt_paged_attend ------------------------------------------------------------
@@ -627,7 +696,9 @@ extern "C" int bpt_paged_attend_noalloc(const void* q, int q_dtype, int64_t q_st
   BPT_REQUIRE(out, BPT_ERR_INVALID, "paged attend (no alloc): null output");
   BPT_REQUIRE(out_dtype == BPT_DTYPE_F32 || out_dtype == BPT_DTYPE_F16 || out_dtype == BPT_DTYPE_BF16,
               BPT_ERR_INVALID, "paged attend (no alloc): out dtype %d", out_dtype);
-  const int64_t need = paged_workspace_bytes(B, Hq, D, n_splits);
+  int64_t cap = 0;
+  const int64_t need = persistent_applies(a, D, cap) ? persist_workspace_bytes(B, Hq, D, num_sms())
+                                                     : split_workspace_bytes(B, Hq, D, n_splits);
   BPT_REQUIRE(need <= kNoAllocBytes, BPT_ERR_WORKSPACE,
               "paged attend (no alloc): B=%lld x n_splits=%lld x Hq=%lld x D=%lld needs %lld bytes of scratch, above the "
               "fixed %lld (use larger splits, or bpt_paged_attend with a caller workspace)",
@@ -640,13 +711,7 @@ extern "C" int bpt_paged_attend_noalloc(const void* q, int q_dtype, int64_t q_st
   cudaError_t err = cudaMemsetAsync(scratch, 0, size_t(B) * sizeof(unsigned int), s);
   if (err != cudaSuccess)
     return set_error(BPT_ERR_CUDA, "paged attend (no alloc): clearing the tickets: %s", cudaGetErrorString(err));
-  uint8_t* ws = static_cast<uint8_t*>(scratch);
-  const int64_t lses = ((B * n_splits * Hq * 4 + 255) / 256) * 256;
-  a.merge = 1;
   a.out = out;
   a.out_dtype = out_dtype;
-  a.ws_count = reinterpret_cast<unsigned int*>(ws);
-  a.ws_lse = reinterpret_cast<float*>(ws + kCounterBytes);
-  a.ws_out = reinterpret_cast<float*>(ws + kCounterBytes + lses);
-  return paged_dispatch(a, kind, D, flags, s);
+  return merge_launch(a, kind, D, flags, s, static_cast<uint8_t*>(scratch), kNoAllocBytes, "paged attend (no alloc)");
 }

@@ -133,8 +133,9 @@ int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_s
  * reference (its attention allocates its partial outputs with torch.empty on every call).
  * The split partials and tickets live in one fixed array of BPT_NOALLOC_SCRATCH_BYTES bytes, a static device
  * variable of this library: every GPU that loads the library holds it until the process exits. A call needs
- * 256 KiB + B * n_splits * Hq * (D + 1) * 4 bytes of it (rounded up to 256 B per part) and returns
- * BPT_ERR_WORKSPACE, launching nothing, when that is more. The first call on a device looks up the array's
+ * 256 KiB + S * Hq * (D + 1) * 4 bytes of it (rounded up to 256 B per part), S = B + the GPU's SM count for
+ * contiguous q with D 64 or 128 and Hkv <= 8, S = B * n_splits otherwise, and returns BPT_ERR_WORKSPACE,
+ * launching nothing, when that is more. The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress) with that device current; make that first call before any stream
  * capture. Each call clears the tickets it uses (an asynchronous memset on `stream`) before the kernel.
  * All calls on a device share the array: calls that overlap on the GPU (concurrent streams) race and corrupt

@@ -64,10 +64,11 @@ def test_no_alloc_attend_matches_the_workspace_entry_point_on_two_calls(kind):
 def test_no_alloc_refuses_a_request_beyond_its_fixed_scratch():
     from bpt_b200 import _lib, workloads
 
-    case = workloads.paged_case("fp8", 2, 16, 8, 128, [64, 64], 16, 16, seed=3, device="cuda")
-    out = torch.zeros(2, 16, 128, device="cuda")
-    # 2 sequences x 8192 splits x 16 heads x 129 floats is far above the 16 MiB array
-    status = call_noalloc(case, 0.1, 16, 8192, out)
+    # 2,100 one-token sequences: at least 2,100 partials of 16 heads x 129 floats, above the 16 MiB array
+    b = 2100
+    case = workloads.paged_case("fp8", b, 16, 8, 128, [1] * b, 16, b, seed=3, device="cuda")
+    out = torch.zeros(b, 16, 128, device="cuda")
+    status = call_noalloc(case, 0.1, 16, 1, out)
     assert status == _lib.ERR_WORKSPACE
     assert b"scratch" in _lib.lib().bpt_last_error()
     assert out.abs().sum() == 0  # nothing was launched
