@@ -65,6 +65,17 @@ __device__ __forceinline__ void word_to_b(uint32_t w, uint32_t& b0, uint32_t& b1
   }
 }
 
+// Four e4m3 codes -> two f16x2 words on the integer pipe: lo = codes (0, 2), hi = codes (1, 3), each 2^-8 times
+// the code's value, exactly. The f16 bits (c & 0x7F) << 7 | (c & 0x80) << 8 put the e4m3 exponent and mantissa
+// into the f16 fields with the exponent bias 8 short (15 - 7); e4m3 subnormals land on f16 subnormals with the
+// same factor. (The conversion instruction does the same work on the quarter-rate conversion unit.)
+__device__ __forceinline__ void e4m3x4_to_f16_scaled(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  constexpr uint32_t m = 0x3F803F80u;  // exponent and mantissa fields of both halves
+  const uint32_t s = w & 0x80808080u;  // sign bits
+  lo = ((w << 7) & m) | ((s << 8) & ~m);
+  hi = ((w >> 1) & m) | (s & ~m);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

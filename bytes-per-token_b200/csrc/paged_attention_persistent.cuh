@@ -19,6 +19,7 @@
 // are the only global round trips before the producer starts.
 
 constexpr int kPersistMaxSeqs = 4096;
+constexpr int kMaxSmemPerCta = 227 * 1024;  // sm_100 opt-in dynamic shared memory per block
 constexpr int kPersistMaxCtaPages = 4096;
 constexpr int64_t kCounterBytesP = 65536 * 4;  // the ticket counters, at the workspace's start (as paged_attend)
 
@@ -49,35 +50,86 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
 }
 
 
-// The part's partials are all in: out[b] = sum_p w_p out_p / sum_p w_p, w_p = exp(lse_p - max lse), with the
-// consumer threads spread over (query head, dim).
+// The part's partials are all in: out[b] = sum_p w_p out_p / sum_p w_p, w_p = exp(lse_p - max lse). Each
+// consumer thread takes two (query head, 4 dims) items at a time and reads the parts in batches of eight with
+// all loads issued before any is used, folding each batch in with a running maximum.
 template <int D>
-__device__ __forceinline__ void merge_parts(const PagedArgs& a, int b, int64_t s0, int nparts, int tid, int ncons) {
-  for (int i = tid; i < a.Hq * D; i += ncons) {
-    const int hq = i / D, d = i % D;
-    float mx = -CUDART_INF_F;
-    for (int p2 = 0; p2 < nparts; ++p2) mx = fmaxf(mx, __ldcg(&a.ws_lse[(s0 + p2) * a.Hq + hq]));
-    float acc = 0.f, wsum = 0.f;
-    if (mx != -CUDART_INF_F) {
-#pragma unroll 4
-      for (int p2 = 0; p2 < nparts; ++p2) {
-        const float w = expf(__ldcg(&a.ws_lse[(s0 + p2) * a.Hq + hq]) - mx);
-        wsum += w;
-        acc += w * __ldcg(&a.ws_out[((s0 + p2) * a.Hq + hq) * D + d]);
+__device__ __noinline__ void merge_parts(const PagedArgs& a, int b, int64_t s0, int nparts, int tid, int ncons) {
+  constexpr int kBatch = 8;
+  const int items = a.Hq * (D / 4);
+  const int64_t ostride = int64_t(a.Hq) * D;
+  for (int i0 = tid; i0 < items; i0 += 2 * ncons) {
+    bool ok[2];
+    const float* lse[2];
+    const float* po[2];
+    float mx[2], wsum[2];
+    float4 acc[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * ncons;
+      ok[u] = i < items;
+      const int hq = ok[u] ? i / (D / 4) : 0, d = ok[u] ? 4 * (i % (D / 4)) : 0;
+      lse[u] = a.ws_lse + s0 * a.Hq + hq;
+      po[u] = a.ws_out + (s0 * a.Hq + hq) * D + d;
+      mx[u] = -CUDART_INF_F;
+      wsum[u] = 0.f;
+      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int p0 = 0; p0 < nparts; p0 += kBatch) {
+      float lv[2][kBatch];
+      float4 ov[2][kBatch];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const bool v = ok[u] && p0 + j < nparts;
+          lv[u][j] = v ? __ldcg(lse[u] + int64_t(p0 + j) * a.Hq) : -CUDART_INF_F;
+          ov[u][j] = v ? __ldcg(reinterpret_cast<const float4*>(po[u] + (p0 + j) * ostride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float bm = lv[u][0];
+#pragma unroll
+        for (int j = 1; j < kBatch; ++j) bm = fmaxf(bm, lv[u][j]);
+        const float nm = fmaxf(mx[u], bm);
+        if (nm == -CUDART_INF_F) continue;  // no tokens in any part so far
+        const float f = expf(mx[u] - nm);
+        wsum[u] *= f;
+        acc[u].x *= f; acc[u].y *= f; acc[u].z *= f; acc[u].w *= f;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const float w = expf(lv[u][j] - nm);
+          wsum[u] += w;
+          acc[u].x += w * ov[u][j].x; acc[u].y += w * ov[u][j].y; acc[u].z += w * ov[u][j].z; acc[u].w += w * ov[u][j].w;
+        }
+        mx[u] = nm;
       }
     }
-    out_store(a.out, a.out_dtype, ((int64_t)b * a.Hq + hq) * D + d, wsum > 0.f ? acc / wsum : 0.f);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!ok[u]) continue;
+      const int i = i0 + u * ncons;
+      const int64_t o = ((int64_t)b * a.Hq + i / (D / 4)) * D + 4 * (i % (D / 4));
+      out_store(a.out, a.out_dtype, o, wsum[u] > 0.f ? acc[u].x / wsum[u] : 0.f);
+      out_store(a.out, a.out_dtype, o + 1, wsum[u] > 0.f ? acc[u].y / wsum[u] : 0.f);
+      out_store(a.out, a.out_dtype, o + 2, wsum[u] > 0.f ? acc[u].z / wsum[u] : 0.f);
+      out_store(a.out, a.out_dtype, o + 3, wsum[u] > 0.f ? acc[u].w / wsum[u] : 0.f);
+    }
   }
 }
 
 // Consumers with tokens on the MMA's M dimension (REP <= 4). Per page:
-//   QK   S^T[16 tokens x 8] = K[16 tokens x 16 dims] . Q^T      B columns: hi parts of heads 0..3, then lo parts
-//   PV   O^T[16 dims x 8]  += V^T[16 dims x 16 tokens] . P^T   B columns: f16(p) of heads 0..3, then p - f16(p)
-// so a page costs D/16 MMAs for each product, q is a constant B fragment (D/8 registers) and the output
-// accumulator is D/4 registers. Lane (c, g) owns the columns 2c, 2c+1: heads hA = 2(c & 1), hA + 1, part c >> 1;
-// hi and lo parts of a head meet with one shuffle (lane ^ 2). P goes from the QK layout (tokens on g) to the PV
-// layout (tokens on c) through a small per-warp tile in shared memory.
-template <int D, int REP, int KIND, int COPY>
+//   QK   S^T[16 tokens x 8] = K[16 tokens x 16 dims] . Q^T
+//   PV   O^T[16 dims x 8]  += V^T[16 dims x 16 tokens] . P^T
+// B column n = 2 * head + part: part 0 is the f16 rounding of q (or p), part 1 the f16 rounding of what is left,
+// so the f16 products add up to fp32-grade results. A page costs D/16 MMAs for each product, q is a constant B
+// fragment (D/8 registers) and the output accumulator D/4 registers. Lane (g, c) gets columns 2c and 2c+1 of
+// every C tile: both parts of head c, summed in the lane, so each lane owns one head. P goes from the QK layout
+// (tokens on g) to the PV layout (tokens on c) through a small per-warp tile in shared memory. A step takes one
+// or two pages of the same part as straight-line code, so their load, convert and MMA chains interleave.
+// CONV (FP8 only): bit 0 converts keys, bit 1 values on the integer pipe (2^-8-scaled, codes paired (0, 2) and
+// (1, 3)) instead of the conversion unit.
+template <int D, int REP, int KIND, int COPY, int CONV>
 __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const PersistLayout& lay, uint8_t* stages,
                                                    uint64_t* full, uint64_t* empty, const int* off, const int* slen,
                                                    const int* pblk, const int* pseq, const int* plp, volatile int* misc,
@@ -87,44 +139,224 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
   constexpr int DQ = D / 4;   // key bytes per lane per token
   constexpr int VD = D / 8;   // value bytes (dims) per lane per token
   constexpr int MT = D / 16;  // PV m-tiles
+  constexpr bool kKAlu = KIND == BPT_KV_FP8 && (CONV & 1);
+  constexpr bool kVAlu = KIND == BPT_KV_FP8 && (CONV & 2);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
-  const int h = warp, Hkv = a.Hkv, ncons = 32 * Hkv, cta = blockIdx.x;
+  const int h = warp, Hkv = a.Hkv, ncons = 32 * Hkv, cta = blockIdx.x, nst = a.nst;
   const int q_esize = a.q_dtype == BPT_DTYPE_F32 ? 4 : 2;
-  const int hA = 2 * (c & 1);          // this lane's heads: hA, hA + 1
-  const int ccol = g & 3, cpart = g >> 2;  // the B column this lane feeds: head ccol, part cpart
+  const int bhead = g >> 1, bpart = g & 1;  // the B column this lane feeds
   float* ptile = ptile_all + warp * 32 * 4;
   float qscale = a.sm_scale * kLog2e;
-  if constexpr (KIND == BPT_KV_FP8) qscale *= a.k_scale;
+  if constexpr (KIND == BPT_KV_FP8) qscale *= a.k_scale * (kKAlu ? 256.f : 1.f);
   float vscale = 1.f;
-  if constexpr (KIND == BPT_KV_FP8) vscale = a.v_scale;
+  if constexpr (KIND == BPT_KV_FP8) vscale = a.v_scale * (kVAlu ? 256.f : 1.f);
 
   uint32_t qb[KS][2];
-  float m[2] = {-CUDART_INF_F, -CUDART_INF_F}, l[2] = {0.f, 0.f};
+  float m = -CUDART_INF_F, l = 0.f;
   float o[MT][4];
   int waited = 0;
 
-  auto wait_page = [&](int k) {
+  auto wait_page = [&](int k, int st, uint32_t ph) {
     if (!misc[2]) {
-      if (mbar_wait_warp(&full[k % a.nst], (k / a.nst) & 1))
+      if (mbar_wait_warp(&full[st], ph))
         waited = k + 1;
       else if (lane == 0)
         misc[2] = 1;
     }
   };
 
+  // One step over pages k .. k + NP - 1 (stages st[0 .. NP - 1]) of a sequence of L tokens.
+  auto step = [&](auto npc, int k, const int* st, int L) {
+    constexpr int NP = decltype(npc)::value;
+    const uint8_t* sp[NP];
+    int hi_tok[NP];  // live tokens of the page (0 for a block index outside the pool)
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg) {
+      sp[pg] = stages + st[pg] * lay.stage_bytes;
+      const int blk = pblk[k + pg];
+      hi_tok[pg] = (blk >= 0 && blk < a.num_blocks) ? min(kBS, L - plp[k + pg] * kBS) : 0;
+    }
+
+    // ---- key rows g and g + 8 of each page; this lane's DQ bytes of the warp's head ----
+    uint32_t w[NP][2][DQ / 4];
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint8_t* row = sp[pg] + (g + 8 * r) * lay.kpitch + h * D + c * DQ;
+#pragma unroll
+        for (int v = 0; v < DQ / 16; ++v) {
+          const uint4 u = *reinterpret_cast<const uint4*>(row + 16 * v);
+          w[pg][r][4 * v] = u.x; w[pg][r][4 * v + 1] = u.y; w[pg][r][4 * v + 2] = u.z; w[pg][r][4 * v + 3] = u.w;
+        }
+      }
+    }
+
+    // ---- S^T = K . Q^T, two accumulators per page (even and odd k-steps) ----
+    float acc[NP][2][4];
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[pg][0][e] = acc[pg][1][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int pg = 0; pg < NP; ++pg) {
+        uint32_t af[4];
+        if constexpr (kKAlu) {  // k slots (2c, 2c+1) = dims (0, 2) of the word, (2c+8, 2c+9) = dims (1, 3)
+          e4m3x4_to_f16_scaled(w[pg][0][ks], af[0], af[2]);
+          e4m3x4_to_f16_scaled(w[pg][1][ks], af[1], af[3]);
+        } else {  // k slots (2c, 2c+1) = dims (0, 1) of the word, (2c+8, 2c+9) = dims (2, 3)
+          word_to_b<KIND>(w[pg][0][ks], af[0], af[2]);  // token g
+          word_to_b<KIND>(w[pg][1][ks], af[1], af[3]);  // token g + 8
+        }
+        mma_f16(acc[pg][ks & 1], af, qb[ks][0], qb[ks][1]);
+      }
+    }
+    float s[NP][2];  // head c at tokens g and g + 8, log2 units
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg) {
+      const float v0 = (acc[pg][0][0] + acc[pg][0][1]) + (acc[pg][1][0] + acc[pg][1][1]);
+      const float v1 = (acc[pg][0][2] + acc[pg][0][3]) + (acc[pg][1][2] + acc[pg][1][3]);
+      const bool live0 = g < hi_tok[pg], live1 = g + 8 < hi_tok[pg];
+      float k0 = qscale, k1 = qscale;
+      if constexpr (KIND == BPT_KV_INT8) {
+        const __half* kscl = reinterpret_cast<const __half*>(sp[pg] + lay.kpage + lay.vpage);
+        k0 *= live0 ? __half2float(kscl[g * Hkv + h]) : 0.f;
+        k1 *= live1 ? __half2float(kscl[(g + 8) * Hkv + h]) : 0.f;
+      }
+      s[pg][0] = live0 ? v0 * k0 : -CUDART_INF_F;
+      s[pg][1] = live1 ? v1 * k1 : -CUDART_INF_F;
+    }
+
+    // ---- online softmax of head c over the step's tokens (the lanes with this c) ----
+    float pm = fmaxf(s[0][0], s[0][1]);
+#pragma unroll
+    for (int pg = 1; pg < NP; ++pg) pm = fmaxf(pm, fmaxf(s[pg][0], s[pg][1]));
+    pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
+    pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
+    pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
+    const float m_new = fmaxf(m, pm);
+    const float m_use = (m_new == -CUDART_INF_F) ? 0.f : m_new;
+    const float alpha = exp2f(m - m_use);
+    float ps = 0.f;
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg) {
+      s[pg][0] = exp2f(s[pg][0] - m_use);
+      s[pg][1] = exp2f(s[pg][1] - m_use);
+      ps += s[pg][0] + s[pg][1];
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    l = l * alpha + ps;
+    m = m_new;
+    if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        o[mt][0] *= alpha; o[mt][1] *= alpha; o[mt][2] *= alpha; o[mt][3] *= alpha;
+      }
+    }
+
+    // ---- P through the warp's tile [token][head] (INT8: times the value scale) ----
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg) {
+      float vs0 = 1.f, vs1 = 1.f;
+      if constexpr (KIND == BPT_KV_INT8) {
+        const __half* vscl = reinterpret_cast<const __half*>(sp[pg] + lay.kpage + lay.vpage + a.scale_bytes);
+        vs0 = g < hi_tok[pg] ? __half2float(vscl[g * Hkv + h]) : 0.f;
+        vs1 = g + 8 < hi_tok[pg] ? __half2float(vscl[(g + 8) * Hkv + h]) : 0.f;
+      }
+      ptile[(pg * 16 + g) * 4 + c] = s[pg][0] * vs0;
+      ptile[(pg * 16 + g + 8) * 4 + c] = s[pg][1] * vs1;
+    }
+    __syncwarp();
+
+    // ---- O^T += V^T . P^T: value rows of tokens 2c, 2c+1, 2c+8, 2c+9; dims [g*VD, (g+1)*VD) ----
+#pragma unroll
+    for (int pg = 0; pg < NP; ++pg) {
+      const uint8_t* vp = sp[pg] + lay.kpage;
+      float pw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pw[j] = ptile[(pg * 16 + 2 * c + (j & 1) + 8 * (j >> 1)) * 4 + bhead];
+      uint32_t b0, b1;
+      {
+        uint32_t h01, l01, h23, l23;
+        split2(pw[0], pw[1], h01, l01);
+        split2(pw[2], pw[3], h23, l23);
+        b0 = bpart ? l01 : h01;
+        b1 = bpart ? l23 : h23;
+      }
+      uint32_t vr[4][VD / 4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint8_t* row = vp + (2 * c + (j & 1) + 8 * (j >> 1)) * lay.vpitch + h * D + g * VD;
+        if constexpr (VD == 16) {
+          const uint4 u = *reinterpret_cast<const uint4*>(row);
+          vr[j][0] = u.x; vr[j][1] = u.y; vr[j][2] = u.z; vr[j][3] = u.w;
+        } else {
+          const uint2 u = *reinterpret_cast<const uint2*>(row);
+          vr[j][0] = u.x; vr[j][1] = u.y;
+        }
+      }
+      if constexpr (KIND == BPT_KV_FP8) {
+        if (hi_tok[pg] < kBS) {  // rows past the sequence may hold NaN codes; int8 codes are all finite
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const bool live = 2 * c + (j & 1) + 8 * (j >> 1) < hi_tok[pg];
+#pragma unroll
+            for (int q = 0; q < VD / 4; ++q) vr[j][q] = live ? vr[j][q] : 0u;
+          }
+        }
+      }
+      uint32_t p01[VD], p89[VD];  // f16x2 (token pair) per lane dim
+#pragma unroll
+      for (int q = 0; q < VD / 4; ++q) {
+        if constexpr (kVAlu) {  // [t0 d0, t0 d1, t1 d0, t1 d1] -> (t0, t1) of d0 and of d1
+          e4m3x4_to_f16_scaled(__byte_perm(vr[0][q], vr[1][q], 0x5410u), p01[4 * q], p01[4 * q + 1]);
+          e4m3x4_to_f16_scaled(__byte_perm(vr[0][q], vr[1][q], 0x7632u), p01[4 * q + 2], p01[4 * q + 3]);
+          e4m3x4_to_f16_scaled(__byte_perm(vr[2][q], vr[3][q], 0x5410u), p89[4 * q], p89[4 * q + 1]);
+          e4m3x4_to_f16_scaled(__byte_perm(vr[2][q], vr[3][q], 0x7632u), p89[4 * q + 2], p89[4 * q + 3]);
+        } else {  // [t0 d0, t1 d0, t0 d1, t1 d1] -> (t0, t1) of d0 and of d1
+          word_to_b<KIND>(__byte_perm(vr[0][q], vr[1][q], 0x5140u), p01[4 * q], p01[4 * q + 1]);
+          word_to_b<KIND>(__byte_perm(vr[0][q], vr[1][q], 0x7362u), p01[4 * q + 2], p01[4 * q + 3]);
+          word_to_b<KIND>(__byte_perm(vr[2][q], vr[3][q], 0x5140u), p89[4 * q], p89[4 * q + 1]);
+          word_to_b<KIND>(__byte_perm(vr[2][q], vr[3][q], 0x7362u), p89[4 * q + 2], p89[4 * q + 3]);
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint32_t af[4] = {p01[mt], p01[VD / 2 + mt], p89[mt], p89[VD / 2 + mt]};
+        mma_f16(o[mt], af, b0, b1);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+      for (int pg = 0; pg < NP; ++pg) mbar_arrive(&empty[st[pg]]);
+    }
+  };
+
+  int st0 = 0;       // stage of page k
+  uint32_t ph = 0;   // its full-barrier parity
   for (int k = 0; k < n;) {
     const int b = pseq[k];
     const bool first = (k == 0) || (pseq[k - 1] != b);
     const int np = (k + 1 < n && pseq[k + 1] == b) ? 2 : 1;
     const bool last = (k + np >= n) || (pseq[k + np] != b);
     const int L = slen[b];
-    wait_page(k);
-    if (np == 2) wait_page(k + 1);
+    int st[2];
+    uint32_t phs[2];
+    st[0] = st0; phs[0] = ph;
+    st[1] = st0 + 1 == nst ? 0 : st0 + 1;
+    phs[1] = st0 + 1 == nst ? ph ^ 1u : ph;
+    wait_page(k, st[0], phs[0]);
+    if (np == 2) wait_page(k + 1, st[1], phs[1]);
 
-    if (first) {  // q of this sequence as the QK B fragment: column g = head ccol, hi or lo part
-      const uint8_t* qrow = stages + (k % a.nst) * lay.stage_bytes + lay.q_off +
-                            (int64_t)(h * REP + (ccol < REP ? ccol : 0)) * D * q_esize;
+    if (first) {  // q of this sequence as the QK B fragment: column g = head g / 2, part g % 2
+      const uint8_t* qrow = stages + st0 * lay.stage_bytes + lay.q_off +
+                            (int64_t)(h * REP + (bhead < REP ? bhead : 0)) * D * q_esize;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         float x[4];
@@ -142,211 +374,57 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
             x[2] = __half2float(__ushort_as_half(uint16_t(v.y & 0xFFFFu))); x[3] = __half2float(__ushort_as_half(uint16_t(v.y >> 16)));
           }
         }
-        if (ccol >= REP) x[0] = x[1] = x[2] = x[3] = 0.f;
+        if (bhead >= REP) x[0] = x[1] = x[2] = x[3] = 0.f;
         uint32_t hi01, lo01, hi23, lo23;
-        split2(x[0], x[1], hi01, lo01);
-        split2(x[2], x[3], hi23, lo23);
-        qb[ks][0] = cpart ? lo01 : hi01;
-        qb[ks][1] = cpart ? lo23 : hi23;
+        if constexpr (kKAlu) {  // the keys' pairing: dims (0, 2) and (1, 3)
+          split2(x[0], x[2], hi01, lo01);
+          split2(x[1], x[3], hi23, lo23);
+        } else {
+          split2(x[0], x[1], hi01, lo01);
+          split2(x[2], x[3], hi23, lo23);
+        }
+        qb[ks][0] = bpart ? lo01 : hi01;
+        qb[ks][1] = bpart ? lo23 : hi23;
       }
-      m[0] = m[1] = -CUDART_INF_F;
-      l[0] = l[1] = 0.f;
+      m = -CUDART_INF_F;
+      l = 0.f;
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     }
 
-    // ---- QK^T: scores of heads hA, hA+1 at tokens g and g+8 of each page ----
-    float s[2][4];  // [page][token g: hA, hA+1, token g+8: hA, hA+1]
-    bool usable[2] = {false, false};
-    int hi_tok[2] = {0, 0};
-#pragma unroll
-    for (int pg = 0; pg < 2; ++pg) {
-      s[pg][0] = s[pg][1] = s[pg][2] = s[pg][3] = -CUDART_INF_F;
-      if (pg < np) {
-        const int kk = k + pg;
-        const uint8_t* kp = stages + (kk % a.nst) * lay.stage_bytes;
-        const __half* kscl = reinterpret_cast<const __half*>(kp + lay.kpage + lay.vpage);
-        usable[pg] = pblk[kk] >= 0 && pblk[kk] < a.num_blocks;
-        hi_tok[pg] = min(kBS, L - plp[kk] * kBS);
-        const uint8_t* r0 = kp + g * lay.kpitch + h * D + c * DQ;
-        const uint8_t* r1 = kp + (g + 8) * lay.kpitch + h * D + c * DQ;
-        uint32_t w0[DQ / 4], w1[DQ / 4];
-#pragma unroll
-        for (int v = 0; v < DQ / 16; ++v) {
-          const uint4 u0 = *reinterpret_cast<const uint4*>(r0 + 16 * v);
-          const uint4 u1 = *reinterpret_cast<const uint4*>(r1 + 16 * v);
-          w0[4 * v] = u0.x; w0[4 * v + 1] = u0.y; w0[4 * v + 2] = u0.z; w0[4 * v + 3] = u0.w;
-          w1[4 * v] = u1.x; w1[4 * v + 1] = u1.y; w1[4 * v + 2] = u1.z; w1[4 * v + 3] = u1.w;
-        }
-        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          uint32_t af[4];
-          word_to_b<KIND>(w0[ks], af[0], af[2]);  // token g: slots (2c, 2c+1) and (2c+8, 2c+9)
-          word_to_b<KIND>(w1[ks], af[1], af[3]);  // token g+8
-          mma_f16(acc[ks & 1], af, qb[ks][0], qb[ks][1]);
-        }
-        float v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[e] = acc[0][e] + acc[1][e];
-          v[e] += __shfl_xor_sync(0xffffffffu, v[e], 2);  // hi + lo parts of the head
-        }
-        const bool live0 = usable[pg] && g < hi_tok[pg];
-        const bool live1 = usable[pg] && g + 8 < hi_tok[pg];
-        float k0 = qscale, k1 = qscale;
-        if constexpr (KIND == BPT_KV_INT8) {
-          k0 *= live0 ? __half2float(kscl[g * Hkv + h]) : 0.f;
-          k1 *= live1 ? __half2float(kscl[(g + 8) * Hkv + h]) : 0.f;
-        }
-        s[pg][0] = live0 ? v[0] * k0 : -CUDART_INF_F;
-        s[pg][1] = live0 ? v[1] * k0 : -CUDART_INF_F;
-        s[pg][2] = live1 ? v[2] * k1 : -CUDART_INF_F;
-        s[pg][3] = live1 ? v[3] * k1 : -CUDART_INF_F;
-      }
-    }
-
-    // ---- online softmax for heads hA, hA+1 over the step's tokens (lanes with the same c) ----
-    float alpha[2];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float pm = fmaxf(fmaxf(s[0][hh], s[0][2 + hh]), fmaxf(s[1][hh], s[1][2 + hh]));
-      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
-      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
-      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
-      const float m_new = fmaxf(m[hh], pm);
-      const float m_use = (m_new == -CUDART_INF_F) ? 0.f : m_new;
-      alpha[hh] = exp2f(m[hh] - m_use);
-      float ps = 0.f;
-#pragma unroll
-      for (int pg = 0; pg < 2; ++pg) {
-        s[pg][hh] = exp2f(s[pg][hh] - m_use);
-        s[pg][2 + hh] = exp2f(s[pg][2 + hh] - m_use);
-        ps += s[pg][hh] + s[pg][2 + hh];
-      }
-      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-      l[hh] = l[hh] * alpha[hh] + ps;
-      m[hh] = m_new;
-    }
-    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        o[mt][0] *= alpha[0]; o[mt][2] *= alpha[0];
-        o[mt][1] *= alpha[1]; o[mt][3] *= alpha[1];
-      }
-    }
-
-    // ---- P through the warp's tile: [token][head], written by the hi-part lanes (INT8: times the value scale) ----
-    if (c < 2) {
-#pragma unroll
-      for (int pg = 0; pg < 2; ++pg) {
-        if (pg < np) {
-          float vs0 = 1.f, vs1 = 1.f;
-          if constexpr (KIND == BPT_KV_INT8) {
-            const uint8_t* kp = stages + ((k + pg) % a.nst) * lay.stage_bytes;
-            const __half* vscl = reinterpret_cast<const __half*>(kp + lay.kpage + lay.vpage + a.scale_bytes);
-            vs0 = (usable[pg] && g < hi_tok[pg]) ? __half2float(vscl[g * Hkv + h]) : 0.f;
-            vs1 = (usable[pg] && g + 8 < hi_tok[pg]) ? __half2float(vscl[(g + 8) * Hkv + h]) : 0.f;
-          }
-          *reinterpret_cast<float2*>(ptile + (pg * 16 + g) * 4 + hA) = make_float2(s[pg][0] * vs0, s[pg][1] * vs0);
-          *reinterpret_cast<float2*>(ptile + (pg * 16 + g + 8) * 4 + hA) = make_float2(s[pg][2] * vs1, s[pg][3] * vs1);
-        }
-      }
-    }
-    __syncwarp();
-
-    // ---- PV^T: value rows of tokens 2c, 2c+1, 2c+8, 2c+9; dims [g*VD, (g+1)*VD) ----
-#pragma unroll
-    for (int pg = 0; pg < 2; ++pg) {
-      if (pg < np && usable[pg]) {
-        const uint8_t* vp = stages + ((k + pg) % a.nst) * lay.stage_bytes + lay.kpage;
-        const int tok[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
-        float pw[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) pw[j] = ptile[(pg * 16 + tok[j]) * 4 + ccol];
-        uint32_t b0, b1;
-        {
-          uint32_t h01, l01, h23, l23;
-          split2(pw[0], pw[1], h01, l01);
-          split2(pw[2], pw[3], h23, l23);
-          b0 = cpart ? l01 : h01;
-          b1 = cpart ? l23 : h23;
-        }
-        uint32_t vr[4][VD / 4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint8_t* row = vp + tok[j] * lay.vpitch + h * D + g * VD;
-          if constexpr (VD == 16) {
-            const uint4 u = *reinterpret_cast<const uint4*>(row);
-            vr[j][0] = u.x; vr[j][1] = u.y; vr[j][2] = u.z; vr[j][3] = u.w;
-          } else {
-            const uint2 u = *reinterpret_cast<const uint2*>(row);
-            vr[j][0] = u.x; vr[j][1] = u.y;
-          }
-          if (!(tok[j] < hi_tok[pg])) {  // rows past the sequence may hold any bytes
-#pragma unroll
-            for (int w = 0; w < VD / 4; ++w) vr[j][w] = 0u;
-          }
-        }
-        uint32_t p01[VD], p89[VD];  // f16x2 (token pair) per lane dim
-#pragma unroll
-        for (int w = 0; w < VD / 4; ++w) {
-          word_to_b<KIND>(__byte_perm(vr[0][w], vr[1][w], 0x5140u), p01[4 * w], p01[4 * w + 1]);
-          word_to_b<KIND>(__byte_perm(vr[0][w], vr[1][w], 0x7362u), p01[4 * w + 2], p01[4 * w + 3]);
-          word_to_b<KIND>(__byte_perm(vr[2][w], vr[3][w], 0x5140u), p89[4 * w], p89[4 * w + 1]);
-          word_to_b<KIND>(__byte_perm(vr[2][w], vr[3][w], 0x7362u), p89[4 * w + 2], p89[4 * w + 3]);
-        }
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const uint32_t af[4] = {p01[mt], p01[VD / 2 + mt], p89[mt], p89[VD / 2 + mt]};
-          mma_f16(o[mt], af, b0, b1);
-        }
-      }
-    }
-    __syncwarp();
-
-    // ---- release the step's stages ----
-    if (lane == 0) {
-      mbar_arrive(&empty[k % a.nst]);
-      if (np == 2) mbar_arrive(&empty[(k + 1) % a.nst]);
-    }
+    if (np == 2)
+      step(std::integral_constant<int, 2>(), k, st, L);
+    else
+      step(std::integral_constant<int, 1>(), k, st, L);
     k += np;
+    st0 = np == 2 ? st[1] : st[0];
+    ph = np == 2 ? phs[1] : phs[0];
+    if (++st0 == nst) { st0 = 0; ph ^= 1u; }
     if (!last) continue;
 
-    // ---- end of a part ----
+    // ---- end of a part: lane (g, c) holds head c at dims g*VD + [0, VD) ----
     const int first_cta = off[b] / per;
     const int last_cta = (off[b + 1] - 1) / per;
     const int nparts = last_cta - first_cta + 1;
+    if (c < REP) {
+      const int hq = h * REP + c;
+      const float inv = l > 0.f ? vscale / l : 0.f;
+      const float lse = l > 0.f ? (m + log2f(l)) * kLn2 : -CUDART_INF_F;
+      float res[VD];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt) {
+        res[mt] = (o[mt][0] + o[mt][1]) * inv;
+        res[VD / 2 + mt] = (o[mt][2] + o[mt][3]) * inv;
+      }
+      if (nparts == 1) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) o[mt][e] += __shfl_xor_sync(0xffffffffu, o[mt][e], 2);
-    if (c < 2) {
+        for (int j = 0; j < VD; ++j) out_store(a.out, a.out_dtype, ((int64_t)b * a.Hq + hq) * D + g * VD + j, res[j]);
+      } else {
+        const int64_t slot = cta + b;
+        float* dst = a.ws_out + (slot * a.Hq + hq) * D + g * VD;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int head = hA + hh;
-        if (head >= REP) continue;
-        const int hq = h * REP + head;
-        const float inv = l[hh] > 0.f ? vscale / l[hh] : 0.f;
-        const float lse = l[hh] > 0.f ? (m[hh] + log2f(l[hh])) * kLn2 : -CUDART_INF_F;
-        float res[VD];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          res[mt] = o[mt][hh] * inv;
-          res[VD / 2 + mt] = o[mt][2 + hh] * inv;
-        }
-        if (nparts == 1) {
-#pragma unroll
-          for (int j = 0; j < VD; ++j) out_store(a.out, a.out_dtype, ((int64_t)b * a.Hq + hq) * D + g * VD + j, res[j]);
-        } else {
-          const int64_t slot = cta + b;
-          float* dst = a.ws_out + (slot * a.Hq + hq) * D + g * VD;
-#pragma unroll
-          for (int j = 0; j < VD; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(res[j], res[j + 1], res[j + 2], res[j + 3]);
-          if (g == 0) a.ws_lse[slot * a.Hq + hq] = lse;
-        }
+        for (int j = 0; j < VD; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(res[j], res[j + 1], res[j + 2], res[j + 3]);
+        if (g == 0) a.ws_lse[slot * a.Hq + hq] = lse;
       }
     }
     if (nparts == 1) continue;
@@ -363,11 +441,11 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
   }
   if (misc[2] && warp == 0 && lane == 0) {
     const int issued = misc[1];
-    for (int k = waited; k < issued; ++k) (void)mbar_wait(&full[k % a.nst], (k / a.nst) & 1, 20000000ull);
+    for (int k = waited; k < issued; ++k) (void)mbar_wait(&full[k % nst], (k / nst) & 1, 20000000ull);
   }
 }
 
-template <int D, int REP, int KIND, int COPY, bool TR>
+template <int D, int REP, int KIND, int COPY, bool TR, int CONV>
 __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persistent_kernel(const PagedArgs a) {
   constexpr int KS = D / 16, DQ = D / 4, VB = D / 8;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -442,9 +520,10 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
     plp[k] = lp;
     pblk[k] = a.block_table[(int64_t)lo * a.bt_stride + lp];
   }
-  if (cta == 0)  // a sequence with no tokens gets a zero output and is in nobody's range
-    for (int i = tid; i < B * a.Hq * D; i += blockDim.x)
-      if (off[i / (a.Hq * D) + 1] == off[i / (a.Hq * D)]) out_store(a.out, a.out_dtype, i, 0.f);
+  // A sequence with no tokens is in nobody's range and gets a zero output: sequence b from CTA b mod G, one warp each.
+  for (int b = cta + G * warp; b < B; b += G * (blockDim.x >> 5))
+    if (off[b + 1] == off[b])
+      for (int i = lane; i < a.Hq * D; i += 32) out_store(a.out, a.out_dtype, (int64_t)b * a.Hq * D + i, 0.f);
   __syncthreads();
   if (n <= 0) return;
 
@@ -452,10 +531,11 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
   if (producer) {
     // ---------------- producer warp ----------------
     const uint64_t policy = l2_policy_evict_first();
-    for (int k = 0; k < n; ++k) {
-      const int st = k % a.nst;
+    int st = 0;        // stage of page k
+    uint32_t eph = 1;  // parity of the empty phase that frees it: (k / nst - 1) & 1
+    for (int k = 0; k < n; ++k, st = (st + 1 == a.nst) ? 0 : st + 1, eph ^= (st == 0) ? 1u : 0u) {
       if (misc[2]) break;
-      if (k >= a.nst && !mbar_wait_warp(&empty[st], ((k / a.nst) - 1) & 1)) {
+      if (k >= a.nst && !mbar_wait_warp(&empty[st], eph)) {
         misc[2] = 1;
         break;
       }
@@ -504,7 +584,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
 
   // ---------------- consumer warps: one per KV head ----------------
   if constexpr (TR) {
-    consume_transposed<D, REP, KIND, COPY>(a, lay, stages, full, empty, off, slen, pblk, pseq, plp, misc, ptile, n, per);
+    consume_transposed<D, REP, KIND, COPY, CONV>(a, lay, stages, full, empty, off, slen, pblk, pseq, plp, misc, ptile, n, per);
     return;
   } else {
   // A step covers one page, or two consecutive pages of the same part (32 tokens): the two pages' QK chains and
@@ -746,23 +826,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
     consumer_sync(ncons);
     if (misc[0] == nparts - 1) {
       __threadfence();
-      // out[b, hq, d] = sum_parts w_p * out_p / sum_parts w_p, w_p = exp(lse_p - max lse); consumer threads over (hq, d)
-      const int64_t s0 = first_cta + b;
-      for (int i = tid; i < a.Hq * D; i += ncons) {
-        const int hq = i / D, d = i % D;
-        float mx = -CUDART_INF_F;
-        for (int p2 = 0; p2 < nparts; ++p2) mx = fmaxf(mx, __ldcg(&a.ws_lse[(s0 + p2) * a.Hq + hq]));
-        float acc = 0.f, wsum = 0.f;
-        if (mx != -CUDART_INF_F) {
-#pragma unroll 4
-          for (int p2 = 0; p2 < nparts; ++p2) {
-            const float w = expf(__ldcg(&a.ws_lse[(s0 + p2) * a.Hq + hq]) - mx);
-            wsum += w;
-            acc += w * __ldcg(&a.ws_out[((s0 + p2) * a.Hq + hq) * D + d]);
-          }
-        }
-        out_store(a.out, a.out_dtype, ((int64_t)b * a.Hq + hq) * D + d, wsum > 0.f ? acc / wsum : 0.f);
-      }
+      merge_parts<D>(a, b, first_cta + b, nparts, tid, ncons);
       if (tid == 0) a.ws_count[b] = 0u;
     }
     consumer_sync(ncons);
@@ -781,20 +845,40 @@ int64_t persist_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int sms) {
   return kCounterBytesP + ((slots * Hq * 4 + 255) / 256) * 256 + ((slots * Hq * D * 4 + 255) / 256) * 256;
 }
 
-template <int D, int REP, int KIND, int COPY>
+using PersistKernel = void (*)(PagedArgs);
+
+// The kernel for (D, REP, KIND): up to four query heads per KV head take the transposed consumers, eight the
+// head-major ones. FP8 converts on the conversion unit (CONV 0) unless BPT_PAGED_CONV picks another split.
+template <int D, int REP, int KIND>
+PersistKernel persist_kernel() {
+  if constexpr (REP <= 4) {
+    if constexpr (KIND == BPT_KV_FP8) {
+      static const int conv = env_int("BPT_PAGED_CONV", 0);
+      if constexpr (D == 128 && REP == 2) {
+        if (conv == 0) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 0>;
+        if (conv == 1) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 1>;
+        if (conv == 2) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 2>;
+      }
+      return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 3>;
+    } else {
+      return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 0>;
+    }
+  } else {
+    return paged_attn_persistent_kernel<D, REP, KIND, 0, false, 0>;
+  }
+}
+
+template <int D, int REP, int KIND>
 int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
-  static const int transposed = env_int("BPT_PAGED_TRANSPOSED", 1);
-  constexpr bool kTR = REP <= 4;
   PagedArgs a = a0;
   const int q_esize = a.q_dtype == BPT_DTYPE_F32 ? 4 : 2;
-  const PersistLayout lay = persist_layout<D, COPY>(a.Hkv, a.Hq, q_esize, a.scale_bytes);
+  const PersistLayout lay = persist_layout<D, 0>(a.Hkv, a.Hq, q_esize, a.scale_bytes);
   const int G = a.persist_ctas;
-  const int fixed = 2 * 8 * 8 + 4 * (2 * a.B + 1) + 12 * a.max_cta_pages + 16 + 16 + a.Hkv * 32 * 4 * 4;
-  a.nst = max(2, min(env_int("BPT_PAGED_STAGES", 5), (210 * 1024 - fixed) / lay.stage_bytes));
-  const int smem = a.nst * lay.stage_bytes + 2 * 8 * a.nst + 4 * (2 * a.B + 1) + 12 * a.max_cta_pages + 16 + 16 +
-                   a.Hkv * 32 * 4 * 4;
-  auto kernel = (kTR && transposed) ? paged_attn_persistent_kernel<D, REP, KIND, COPY, kTR>
-                                    : paged_attn_persistent_kernel<D, REP, KIND, COPY, false>;
+  // Everything but the stages and their two barriers: offsets, lengths, page lists, misc, the P tiles.
+  const int fixed = 4 * (2 * a.B + 1) + 12 * a.max_cta_pages + 16 + 16 + a.Hkv * 32 * 4 * 4;
+  a.nst = max(2, min(min(env_int("BPT_PAGED_STAGES", 5), 8), (kMaxSmemPerCta - fixed) / (lay.stage_bytes + 16)));
+  const int smem = a.nst * (lay.stage_bytes + 16) + fixed;
+  const PersistKernel kernel = persist_kernel<D, REP, KIND>();
   int st = set_max_smem(reinterpret_cast<const void*>(kernel), smem);
   if (st) return st;
   cudaLaunchConfig_t cfg = {};
@@ -812,20 +896,13 @@ int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   return BPT_OK;
 }
 
-template <int D, int KIND, int COPY>
-int launch_persist_rep(const PagedArgs& a, int rep, int flags, cudaStream_t stream) {
-  switch (rep) {
-    case 1: return launch_persist_t<D, 1, KIND, COPY>(a, flags, stream);
-    case 2: return launch_persist_t<D, 2, KIND, COPY>(a, flags, stream);
-    case 4: return launch_persist_t<D, 4, KIND, COPY>(a, flags, stream);
-    case 8: return launch_persist_t<D, 8, KIND, COPY>(a, flags, stream);
-  }
-  return set_error(BPT_ERR_UNSUPPORTED, "paged attention: REP=%d not in {1, 2, 4, 8}", rep);
-}
-
 template <int D, int KIND>
 int launch_persist(const PagedArgs& a, int rep, int flags, cudaStream_t stream) {
-  static const int copy = env_int("BPT_PAGED_PCOPY", 0);
-  if (copy == 3) return launch_persist_rep<D, KIND, 3>(a, rep, flags, stream);
-  return launch_persist_rep<D, KIND, 0>(a, rep, flags, stream);
+  switch (rep) {
+    case 1: return launch_persist_t<D, 1, KIND>(a, flags, stream);
+    case 2: return launch_persist_t<D, 2, KIND>(a, flags, stream);
+    case 4: return launch_persist_t<D, 4, KIND>(a, flags, stream);
+    case 8: return launch_persist_t<D, 8, KIND>(a, flags, stream);
+  }
+  return set_error(BPT_ERR_UNSUPPORTED, "paged attention: REP=%d not in {1, 2, 4, 8}", rep);
 }
