@@ -535,9 +535,11 @@ int paged_dispatch(const PagedArgs& a, int kind, int64_t D, int flags, cudaStrea
 // call leaves behind are found by the next call whatever its shape or kernel.
 //   split kernels:      [counters][lse: B x S x Hq f32][outs: B x S x Hq x D f32]
 //   persistent kernel:  [counters][lse: (B + CTAs) x Hq f32][outs: (B + CTAs) x Hq x D f32]
+// The split kernels count per sequence, the persistent kernel per (sequence, KV head).
 constexpr int64_t kMaxSeqs = 65536;
 constexpr int64_t kCounterBytes = kMaxSeqs * 4;
 static_assert(kCounterBytes == kCounterBytesP, "one counter region for every merge kernel");
+static_assert(int64_t(kPersistMaxSeqs) * kMmaMaxHkv <= kMaxSeqs, "persistent tickets fit the counter region");
 
 int64_t split_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits) {
   const int64_t outs = B * n_splits * Hq * D * 4;
@@ -708,8 +710,10 @@ extern "C" int bpt_paged_attend_noalloc(const void* q, int q_dtype, int64_t q_st
   st = noalloc_scratch(&scratch);
   if (st) return st;
   auto s = static_cast<cudaStream_t>(stream);
-  // The array keeps whatever the last call left: the tickets this call uses must start at zero.
-  cudaError_t err = cudaMemsetAsync(scratch, 0, size_t(B) * sizeof(unsigned int), s);
+  // The array keeps whatever the last call left: the tickets this call uses (one per sequence, or per sequence
+  // and KV head for the persistent kernel) must start at zero.
+  const size_t tickets = size_t(B) * (persistent_applies(a, D, cap) ? size_t(Hkv) : 1u);
+  cudaError_t err = cudaMemsetAsync(scratch, 0, tickets * sizeof(unsigned int), s);
   if (err != cudaSuccess)
     return set_error(BPT_ERR_CUDA, "paged attend (no alloc): clearing the tickets: %s", cudaGetErrorString(err));
   a.out = out;

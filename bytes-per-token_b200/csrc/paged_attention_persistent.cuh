@@ -50,71 +50,52 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
 }
 
 
-// The part's partials are all in: out[b] = sum_p w_p out_p / sum_p w_p, w_p = exp(lse_p - max lse). Each
-// consumer thread takes two (query head, 4 dims) items at a time and reads the parts in batches of eight with
-// all loads issued before any is used, folding each batch in with a running maximum.
+// The part's partials are all in: out[b, hq] = sum_p w_p out_p / sum_p w_p, w_p = exp(lse_p - max lse), for
+// the query heads hq0 .. hq0 + nheads - 1. Each of the group's nthr threads takes one (query head, 4 dims) item at
+// a time and reads the parts in batches of eight with all loads issued before any is used, folding each batch in
+// with a running maximum.
 template <int D>
-__device__ __noinline__ void merge_parts(const PagedArgs& a, int b, int64_t s0, int nparts, int tid, int ncons) {
+__device__ __forceinline__ void merge_parts(const PagedArgs& a, int b, int64_t s0, int nparts, int hq0, int nheads,
+                                            int tid, int nthr) {
   constexpr int kBatch = 8;
-  const int items = a.Hq * (D / 4);
+  const int items = nheads * (D / 4);
   const int64_t ostride = int64_t(a.Hq) * D;
-  for (int i0 = tid; i0 < items; i0 += 2 * ncons) {
-    bool ok[2];
-    const float* lse[2];
-    const float* po[2];
-    float mx[2], wsum[2];
-    float4 acc[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = i0 + u * ncons;
-      ok[u] = i < items;
-      const int hq = ok[u] ? i / (D / 4) : 0, d = ok[u] ? 4 * (i % (D / 4)) : 0;
-      lse[u] = a.ws_lse + s0 * a.Hq + hq;
-      po[u] = a.ws_out + (s0 * a.Hq + hq) * D + d;
-      mx[u] = -CUDART_INF_F;
-      wsum[u] = 0.f;
-      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+  for (int i = tid; i < items; i += nthr) {
+    const int hq = hq0 + i / (D / 4), d = 4 * (i % (D / 4));
+    const float* lse = a.ws_lse + s0 * a.Hq + hq;
+    const float* po = a.ws_out + (s0 * a.Hq + hq) * D + d;
+    float mx = -CUDART_INF_F, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int p0 = 0; p0 < nparts; p0 += kBatch) {
-      float lv[2][kBatch];
-      float4 ov[2][kBatch];
+      float lv[kBatch];
+      float4 ov[kBatch];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-          const bool v = ok[u] && p0 + j < nparts;
-          lv[u][j] = v ? __ldcg(lse[u] + int64_t(p0 + j) * a.Hq) : -CUDART_INF_F;
-          ov[u][j] = v ? __ldcg(reinterpret_cast<const float4*>(po[u] + (p0 + j) * ostride)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float bm = lv[u][0];
-#pragma unroll
-        for (int j = 1; j < kBatch; ++j) bm = fmaxf(bm, lv[u][j]);
-        const float nm = fmaxf(mx[u], bm);
-        if (nm == -CUDART_INF_F) continue;  // no tokens in any part so far
-        const float f = expf(mx[u] - nm);
-        wsum[u] *= f;
-        acc[u].x *= f; acc[u].y *= f; acc[u].z *= f; acc[u].w *= f;
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-          const float w = expf(lv[u][j] - nm);
-          wsum[u] += w;
-          acc[u].x += w * ov[u][j].x; acc[u].y += w * ov[u][j].y; acc[u].z += w * ov[u][j].z; acc[u].w += w * ov[u][j].w;
-        }
-        mx[u] = nm;
+      for (int j = 0; j < kBatch; ++j) {
+        const bool v = p0 + j < nparts;
+        lv[j] = v ? __ldcg(lse + int64_t(p0 + j) * a.Hq) : -CUDART_INF_F;
+        ov[j] = v ? __ldcg(reinterpret_cast<const float4*>(po + (p0 + j) * ostride)) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    }
+      float bm = lv[0];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (!ok[u]) continue;
-      const int i = i0 + u * ncons;
-      const int64_t o = ((int64_t)b * a.Hq + i / (D / 4)) * D + 4 * (i % (D / 4));
-      out_store(a.out, a.out_dtype, o, wsum[u] > 0.f ? acc[u].x / wsum[u] : 0.f);
-      out_store(a.out, a.out_dtype, o + 1, wsum[u] > 0.f ? acc[u].y / wsum[u] : 0.f);
-      out_store(a.out, a.out_dtype, o + 2, wsum[u] > 0.f ? acc[u].z / wsum[u] : 0.f);
-      out_store(a.out, a.out_dtype, o + 3, wsum[u] > 0.f ? acc[u].w / wsum[u] : 0.f);
+      for (int j = 1; j < kBatch; ++j) bm = fmaxf(bm, lv[j]);
+      const float nm = fmaxf(mx, bm);
+      if (nm == -CUDART_INF_F) continue;  // no tokens in any part so far
+      const float f = expf(mx - nm);
+      wsum *= f;
+      acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const float w = expf(lv[j] - nm);
+        wsum += w;
+        acc.x += w * ov[j].x; acc.y += w * ov[j].y; acc.z += w * ov[j].z; acc.w += w * ov[j].w;
+      }
+      mx = nm;
     }
+    const int64_t o = ((int64_t)b * a.Hq + hq) * D + d;
+    out_store(a.out, a.out_dtype, o, wsum > 0.f ? acc.x / wsum : 0.f);
+    out_store(a.out, a.out_dtype, o + 1, wsum > 0.f ? acc.y / wsum : 0.f);
+    out_store(a.out, a.out_dtype, o + 2, wsum > 0.f ? acc.z / wsum : 0.f);
+    out_store(a.out, a.out_dtype, o + 3, wsum > 0.f ? acc.w / wsum : 0.f);
   }
 }
 
@@ -313,16 +294,18 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
       uint32_t p01[VD], p89[VD];  // f16x2 (token pair) per lane dim
 #pragma unroll
       for (int q = 0; q < VD / 4; ++q) {
+        const uint32_t* r = &vr[0][0];
+        constexpr int R = VD / 4;  // words per row
         if constexpr (kVAlu) {  // [t0 d0, t0 d1, t1 d0, t1 d1] -> (t0, t1) of d0 and of d1
-          e4m3x4_to_f16_scaled(__byte_perm(vr[0][q], vr[1][q], 0x5410u), p01[4 * q], p01[4 * q + 1]);
-          e4m3x4_to_f16_scaled(__byte_perm(vr[0][q], vr[1][q], 0x7632u), p01[4 * q + 2], p01[4 * q + 3]);
-          e4m3x4_to_f16_scaled(__byte_perm(vr[2][q], vr[3][q], 0x5410u), p89[4 * q], p89[4 * q + 1]);
-          e4m3x4_to_f16_scaled(__byte_perm(vr[2][q], vr[3][q], 0x7632u), p89[4 * q + 2], p89[4 * q + 3]);
+          e4m3x4_to_f16_scaled(__byte_perm(r[q], r[R + q], 0x5410u), p01[4 * q], p01[4 * q + 1]);
+          e4m3x4_to_f16_scaled(__byte_perm(r[q], r[R + q], 0x7632u), p01[4 * q + 2], p01[4 * q + 3]);
+          e4m3x4_to_f16_scaled(__byte_perm(r[2 * R + q], r[3 * R + q], 0x5410u), p89[4 * q], p89[4 * q + 1]);
+          e4m3x4_to_f16_scaled(__byte_perm(r[2 * R + q], r[3 * R + q], 0x7632u), p89[4 * q + 2], p89[4 * q + 3]);
         } else {  // [t0 d0, t1 d0, t0 d1, t1 d1] -> (t0, t1) of d0 and of d1
-          word_to_b<KIND>(__byte_perm(vr[0][q], vr[1][q], 0x5140u), p01[4 * q], p01[4 * q + 1]);
-          word_to_b<KIND>(__byte_perm(vr[0][q], vr[1][q], 0x7362u), p01[4 * q + 2], p01[4 * q + 3]);
-          word_to_b<KIND>(__byte_perm(vr[2][q], vr[3][q], 0x5140u), p89[4 * q], p89[4 * q + 1]);
-          word_to_b<KIND>(__byte_perm(vr[2][q], vr[3][q], 0x7362u), p89[4 * q + 2], p89[4 * q + 3]);
+          word_to_b<KIND>(__byte_perm(r[q], r[R + q], 0x5140u), p01[4 * q], p01[4 * q + 1]);
+          word_to_b<KIND>(__byte_perm(r[q], r[R + q], 0x7362u), p01[4 * q + 2], p01[4 * q + 3]);
+          word_to_b<KIND>(__byte_perm(r[2 * R + q], r[3 * R + q], 0x5140u), p89[4 * q], p89[4 * q + 1]);
+          word_to_b<KIND>(__byte_perm(r[2 * R + q], r[3 * R + q], 0x7362u), p89[4 * q + 2], p89[4 * q + 3]);
         }
       }
 #pragma unroll
@@ -331,7 +314,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
         mma_f16(o[mt], af, b0, b1);
       }
     }
-    __syncwarp();
+    __syncwarp();  // all reads of the stages and of the P tile are done
     if (lane == 0) {
 #pragma unroll
       for (int pg = 0; pg < NP; ++pg) mbar_arrive(&empty[st[pg]]);
@@ -428,16 +411,22 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
       }
     }
     if (nparts == 1) continue;
-    __threadfence();
-    consumer_sync(ncons);
-    if (tid == 0) misc[0] = int(atomicAdd(&a.ws_count[b], 1u));
-    consumer_sync(ncons);
-    if (misc[0] == nparts - 1) {
+    // Each warp (KV head) takes its own ticket for (sequence, KV head). The warp barrier orders the lanes'
+    // partial writes before lane 0's fence; the fence after the ticket orders the other parts' partials before
+    // the lanes' reads, again through the warp barrier.
+    __syncwarp();
+    int ticket = 0;
+    if (lane == 0) {
       __threadfence();
-      merge_parts<D>(a, b, first_cta + b, nparts, tid, ncons);
-      if (tid == 0) a.ws_count[b] = 0u;
+      ticket = int(atomicAdd(&a.ws_count[int64_t(b) * Hkv + h], 1u));
+      __threadfence();
     }
-    consumer_sync(ncons);
+    __syncwarp();
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket == nparts - 1) {
+      merge_parts<D>(a, b, first_cta + b, nparts, h * REP, REP, lane, 32);
+      if (lane == 0) a.ws_count[int64_t(b) * Hkv + h] = 0u;
+    }
   }
   if (misc[2] && warp == 0 && lane == 0) {
     const int issued = misc[1];
@@ -820,16 +809,22 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
       }
     }
     if (nparts == 1) continue;
-    __threadfence();
-    consumer_sync(ncons);
-    if (tid == 0) misc[0] = int(atomicAdd(&a.ws_count[b], 1u));
-    consumer_sync(ncons);
-    if (misc[0] == nparts - 1) {
+    // Each warp (KV head) takes its own ticket for (sequence, KV head). The warp barrier orders the lanes'
+    // partial writes before lane 0's fence; the fence after the ticket orders the other parts' partials before
+    // the lanes' reads, again through the warp barrier.
+    __syncwarp();
+    int ticket = 0;
+    if (lane == 0) {
       __threadfence();
-      merge_parts<D>(a, b, first_cta + b, nparts, tid, ncons);
-      if (tid == 0) a.ws_count[b] = 0u;
+      ticket = int(atomicAdd(&a.ws_count[int64_t(b) * Hkv + h], 1u));
+      __threadfence();
     }
-    consumer_sync(ncons);
+    __syncwarp();
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket == nparts - 1) {
+      merge_parts<D>(a, b, first_cta + b, nparts, h * REP, REP, lane, 32);
+      if (lane == 0) a.ws_count[int64_t(b) * Hkv + h] = 0u;
+    }
   }
   // After an abort, wait (bounded) for every page the producer issued beyond the last one seen, so no copy
   // lands in shared memory after the CTA is gone.
