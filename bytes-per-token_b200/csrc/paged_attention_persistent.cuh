@@ -45,6 +45,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Atomic add at GPU scope with release (prior writes, and those ordered before by a barrier, are visible first)
+// and acquire (later reads see what the other arrivals released) semantics; returns the old value.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(unsigned int* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
@@ -321,6 +329,23 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
     }
   };
 
+  // A part's ticket (per sequence and KV head) is taken at the part's end and read at the next part's end, or
+  // after the last page, so the warp does not wait for the atomic's round trip between its pages. The last of
+  // a sequence's parts to arrive merges them.
+  int pend_b = -1, pend_nparts = 0;
+  int64_t pend_s0 = 0;
+  uint32_t pend_ticket = 0;
+  auto settle = [&]() {
+    if (pend_b < 0) return;
+    const int t = __shfl_sync(0xffffffffu, int(pend_ticket), 0);
+    __syncwarp();  // lane 0's acquire, then every lane's reads
+    if (t == pend_nparts - 1) {
+      merge_parts<D>(a, pend_b, pend_s0, pend_nparts, h * REP, REP, lane, 32);
+      if (lane == 0) a.ws_count[int64_t(pend_b) * Hkv + h] = 0u;
+    }
+    pend_b = -1;
+  };
+
   int st0 = 0;       // stage of page k
   uint32_t ph = 0;   // its full-barrier parity
   for (int k = 0; k < n;) {
@@ -411,23 +436,14 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
       }
     }
     if (nparts == 1) continue;
-    // Each warp (KV head) takes its own ticket for (sequence, KV head). The warp barrier orders the lanes'
-    // partial writes before lane 0's fence; the fence after the ticket orders the other parts' partials before
-    // the lanes' reads, again through the warp barrier.
-    __syncwarp();
-    int ticket = 0;
-    if (lane == 0) {
-      __threadfence();
-      ticket = int(atomicAdd(&a.ws_count[int64_t(b) * Hkv + h], 1u));
-      __threadfence();
-    }
-    __syncwarp();
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
-    if (ticket == nparts - 1) {
-      merge_parts<D>(a, b, first_cta + b, nparts, h * REP, REP, lane, 32);
-      if (lane == 0) a.ws_count[int64_t(b) * Hkv + h] = 0u;
-    }
+    settle();
+    __syncwarp();  // the lanes' partial writes before lane 0's release
+    if (lane == 0) pend_ticket = atom_add_acq_rel_gpu(&a.ws_count[int64_t(b) * Hkv + h], 1u);
+    pend_b = b;
+    pend_nparts = nparts;
+    pend_s0 = first_cta + b;
   }
+  settle();
   if (misc[2] && warp == 0 && lane == 0) {
     const int issued = misc[1];
     for (int k = waited; k < issued; ++k) (void)mbar_wait(&full[k % nst], (k / nst) & 1, 20000000ull);
