@@ -84,6 +84,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// The same test, letting the hardware suspend the thread until the phase completes or about `ns` nanoseconds
+// pass, so a waiting warp does not take issue slots from the warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -96,8 +110,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0 && global_timer_ns() - start > limit_ns) {
+    if (mbar_try_wait_suspend(bar, parity, 1000u)) return true;
+    if ((i & 15u) == 0 && global_timer_ns() - start > limit_ns) {
       record_error(kDevErrTimeout);
       return false;
     }

@@ -14,6 +14,8 @@
 // two groups):  sum_k x_k * s * (q_k - z) = s * (sum_k x_k * (128 + q_k) - (128 + z) * sum_k x_k).
 // Lanes reduce with shuffles; slices (and, fused, the gate/up row pair) combine in shared memory in a fixed
 // order, so results are deterministic.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace bpt {
@@ -221,9 +223,17 @@ int w4a16_check(const void* x, int64_t ldx, const int32_t* qweight, const void* 
   return BPT_OK;
 }
 
+bool w4a16_mma_applies(int64_t M, int64_t N, int64_t K, int64_t group);
+int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
+              int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
+
+// Small M: the tensor-core kernel (w4a16_mma.cu) where its staging fits, the CUDA-core kernel below otherwise.
 int w4a16_gemv(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                cudaStream_t stream) {
+  static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
+  if (!cuda_cores && w4a16_mma_applies(M, N, K, group))
+    return w4a16_mma(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
   GemvArgs a;
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.ldx = ldx;

@@ -1,0 +1,267 @@
+// W4A16 linear for small M on the tensor cores: y[M, N] = x[M, K] . (scale * (q - zero))^T, M <= 16.
+//
+// One CTA owns 8 weight rows (the MMA's N) and all of K; its four warps split K. The CTA's rows reach shared
+// memory with one bulk copy per row (TMA engine) to a padded pitch, so the lanes' 8-byte reads of the 8 rows
+// fall on different banks. A grid of ceil(N / 8) CTAs (768 for N = 6144) is resident at once, so every row of
+// the matrix is requested at the start and the kernel streams at the rate HBM delivers.
+//
+// mma.sync m16n8k16 bf16 -> fp32, per 16 inputs of K (k-step t):
+//   B[k][n] = 128 + q[n][k]: lane (g, c) turns the two int32 words of row n = g that hold inputs 16t .. 16t+15 into
+//     its B registers with one shift and one LOP3 each: (w >> 4c) & 0x000F000F | 0x43004300 is the bf16 pair
+//     (128 + q[16t + c], 128 + q[16t + c + 4]) exactly (and 16t + 8 + c, 16t + 12 + c from the second word). So
+//     B's k slots (2c, 2c+1, 2c+8, 2c+9) stand for inputs (c, c+4, 8+c, 12+c) of the step.
+//   A[m][k] = x[m] in the same input order, staged once per CTA in shared memory as each lane's register pairs.
+// The zero point and the 128 offset fold into the group sums:
+//   sum_k x_k s (q_k - z) = s (sum_k x_k (128 + q_k) - (128 + z) sum_k x_k),
+// with the MMA accumulating the first sum over a group's steps and the second coming from per-step sums of x.
+// The warps' partial sums meet in shared memory in a fixed order: results are deterministic.
+#include "common.cuh"
+
+namespace bpt {
+namespace {
+
+constexpr int kRows = 8;    // weight rows per CTA
+constexpr int kWarps = 4;   // K split
+constexpr int kMaxM = 16;   // x rows per launch (A has 16 rows)
+constexpr int kSmemLimit = 110 * 1024;  // two CTAs per SM at least
+
+struct MmaArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const uint8_t* qweight;  // [N, K/2] bytes
+  const __half* scales;    // [N, G]
+  const uint32_t* qzeros;  // [N, ZW] or null (symmetric: zero point 8)
+  __nv_bfloat16* y;
+  int64_t ldy;
+  int M, N, K, group, G, ZW;
+  int T;       // k-steps: K / 16
+  int pitch;   // weight row pitch in shared memory: K/2 + 16
+  int xpitch;  // staged x row pitch in bytes: 32 T rounded up to 64, + 64 (rows g and g + 1 on other banks)
+  int spitch;  // x step-sum row pitch in floats: T rounded up to even, + 2
+};
+
+__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t offset_codes(uint32_t w, int c) {
+  return ((w >> (4 * c)) & 0x000F000Fu) | 0x43004300u;
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+template <bool FUSED>
+__global__ void __launch_bounds__(32 * kWarps) w4a16_mma_kernel(const MmaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int row0 = blockIdx.x * kRows;
+  const int nrows = min(kRows, a.N - row0);
+  const int m0 = blockIdx.y * kMaxM;
+  const int mt = min(kMaxM, a.M - m0);
+  const int T = a.T;
+
+  // shared memory: weights [8][pitch] | x pairs [mt][xpitch] | x step sums [mt][spitch] f32 | scales [8][G] f32 |
+  // zeros + 128 [8][G] f32 | partials [warps][16][8] f32 | mbarrier
+  uint8_t* wsm = smem;
+  uint8_t* xq = wsm + kRows * a.pitch;
+  float* xs = reinterpret_cast<float*>(xq + mt * a.xpitch);
+  float* ssm = xs + mt * a.spitch;
+  float* zsm = ssm + kRows * a.G;
+  float* red = zsm + kRows * a.G;
+  uint64_t* bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(red + kWarps * kMaxM * kRows) + 15) &
+                                              ~uintptr_t(15));
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int row_bytes = a.K >> 1;
+  if (tid == 0) {  // the weights do not depend on the previous kernel: request them before waiting on it
+    const uint64_t policy = l2_policy_evict_first();
+    mbar_arrive_expect_tx(bar, uint32_t(nrows * row_bytes));
+    for (int r = 0; r < nrows; ++r)
+      bulk_g2s_evict_first(wsm + r * a.pitch, a.qweight + int64_t(row0 + r) * row_bytes, row_bytes, bar, policy);
+  }
+
+  // Each warp works on k-steps [t0, t1) and stages only what that range needs: the groups' scales and zero
+  // points, then (after the previous kernel is done) x.
+  const int t0 = warp * T / kWarps, t1 = (warp + 1) * T / kWarps;
+  const int spg = a.group >> 4;  // k-steps per group (even: the group is a multiple of 32)
+  const int g0 = t0 / spg, g1 = (t1 + spg - 1) / spg;
+  for (int i = lane; i < kRows * (g1 - g0); i += 32) {
+    const int r = i / (g1 - g0), gi = g0 + i % (g1 - g0);
+    float sc = 0.f, z = 136.f;
+    if (r < nrows) {
+      sc = __half2float(a.scales[int64_t(row0 + r) * a.G + gi]);
+      if (a.qzeros) z = 128.f + float((a.qzeros[int64_t(row0 + r) * a.ZW + (gi >> 3)] >> (4 * (gi & 7))) & 15u);
+    }
+    ssm[r * a.G + gi] = sc;
+    zsm[r * a.G + gi] = z;
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // the activations (and the output) belong to the previous kernel until here
+
+  // x of step t, row m, lane c: the A pairs (x[16t + c], x[16t + c + 4]) and (x[16t + 8 + c], x[16t + 12 + c]),
+  // stored so that a lane reads both of a step pair (t, t + 1) with one 16-byte load; and the step's sum of x.
+  const int nt = t1 - t0;
+  for (int i = lane; i < mt * nt; i += 32) {
+    const int m = i / nt, t = t0 + i % nt;
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + int64_t(m0 + m) * a.ldx + 16 * t);
+    const uint4 u0 = src[0], u1 = src[1];  // inputs 0..7 and 8..15 of the step, as bf16 pairs
+    const uint32_t lo[4] = {u0.x, u0.y, u0.z, u0.w}, hi[4] = {u1.x, u1.y, u1.z, u1.w};
+    float sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      sum += (bf16_bits_to_float(lo[e] & 0xFFFFu) + bf16_bits_to_float(lo[e] >> 16)) +
+             (bf16_bits_to_float(hi[e] & 0xFFFFu) + bf16_bits_to_float(hi[e] >> 16));
+    uint8_t* row = xq + m * a.xpitch + (t >> 1) * 64 + (t & 1) * 8;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      // input j of the step is half (j & 1) of word j >> 1
+      const uint32_t w0 = lo[cc >> 1], w4 = lo[(cc + 4) >> 1], w8 = hi[cc >> 1], w12 = hi[(cc + 4) >> 1];
+      const uint32_t sel = (cc & 1) ? 0x7632u : 0x5410u;  // the high or the low halves of the two words
+      *reinterpret_cast<uint2*>(row + cc * 16) = make_uint2(__byte_perm(w0, w4, sel), __byte_perm(w8, w12, sel));
+    }
+    xs[m * a.spitch + t] = sum;
+  }
+  __syncwarp();
+
+  float total[4] = {0.f, 0.f, 0.f, 0.f};  // D[m = g, g + 8][n = 2c, 2c + 1]
+  if (mbar_wait_warp(bar, 0)) {
+    const uint8_t* wrow = wsm + g * a.pitch;
+    const bool row_a = g < mt, row_b = g + 8 < mt;
+    const uint8_t* xa = xq + g * a.xpitch + c * 16;
+    const uint8_t* xb = xq + (g + 8) * a.xpitch + c * 16;
+    const float* sxa = xs + g * a.spitch;
+    const float* sxb = xs + (g + 8) * a.spitch;
+    const int n0 = 2 * c;
+    for (int grp = g0; grp < g1; ++grp) {
+      const int ta = max(t0, grp * spg), tb = min(t1, (grp + 1) * spg);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float sa = 0.f, sb = 0.f;  // sums of x over the steps folded here, rows g and g + 8
+      int t = ta;
+      auto one_step = [&](int tt) {
+        const uint2 wv = *reinterpret_cast<const uint2*>(wrow + 8 * tt);
+        const uint2 pa = row_a ? *reinterpret_cast<const uint2*>(xa + (tt >> 1) * 64 + (tt & 1) * 8) : make_uint2(0u, 0u);
+        const uint2 pb = row_b ? *reinterpret_cast<const uint2*>(xb + (tt >> 1) * 64 + (tt & 1) * 8) : make_uint2(0u, 0u);
+        sa += row_a ? sxa[tt] : 0.f;
+        sb += row_b ? sxb[tt] : 0.f;
+        mma_bf16(acc, pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
+      };
+      if (t & 1) one_step(t++);
+      for (; t + 2 <= tb; t += 2) {  // a step pair: one 16-byte load each of weights and x
+        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + 8 * t);
+        const uint4 pa = row_a ? *reinterpret_cast<const uint4*>(xa + (t >> 1) * 64) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 pb = row_b ? *reinterpret_cast<const uint4*>(xb + (t >> 1) * 64) : make_uint4(0u, 0u, 0u, 0u);
+        const float2 qa = row_a ? *reinterpret_cast<const float2*>(sxa + t) : make_float2(0.f, 0.f);
+        const float2 qb = row_b ? *reinterpret_cast<const float2*>(sxb + t) : make_float2(0.f, 0.f);
+        sa += qa.x + qa.y;
+        sb += qb.x + qb.y;
+        mma_bf16(acc, pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
+        mma_bf16(acc, pa.z, pb.z, pa.w, pb.w, offset_codes(wv.z, c), offset_codes(wv.w, c));
+      }
+      if (t < tb) one_step(t);
+      const float s0 = ssm[n0 * a.G + grp], s1 = ssm[(n0 + 1) * a.G + grp];
+      const float z0 = zsm[n0 * a.G + grp], z1 = zsm[(n0 + 1) * a.G + grp];
+      total[0] += s0 * (acc[0] - z0 * sa);
+      total[1] += s1 * (acc[1] - z1 * sa);
+      total[2] += s0 * (acc[2] - z0 * sb);
+      total[3] += s1 * (acc[3] - z1 * sb);
+    }
+  }
+  float* rw = red + warp * kMaxM * kRows;
+  rw[g * kRows + 2 * c] = total[0];
+  rw[g * kRows + 2 * c + 1] = total[1];
+  rw[(g + 8) * kRows + 2 * c] = total[2];
+  rw[(g + 8) * kRows + 2 * c + 1] = total[3];
+  __syncthreads();
+  if (tid == 0) (void)mbar_wait(bar, 0, 50000000ull);  // every copy has landed before the CTA exits (bounded)
+  if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
+    for (int i = tid; i < mt * (kRows / 2); i += blockDim.x) {
+      const int m = i / (kRows / 2), p = i % (kRows / 2);
+      if (2 * p + 1 >= nrows) continue;
+      float gs = 0.f, us = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        gs += red[(w * kMaxM + m) * kRows + 2 * p];
+        us += red[(w * kMaxM + m) * kRows + 2 * p + 1];
+      }
+      a.y[int64_t(m0 + m) * a.ldy + (row0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
+    }
+  } else {
+    for (int i = tid; i < mt * kRows; i += blockDim.x) {
+      const int m = i / kRows, n = i % kRows;
+      if (n >= nrows) continue;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) sum += red[(w * kMaxM + m) * kRows + n];
+      a.y[int64_t(m0 + m) * a.ldy + row0 + n] = __float2bfloat16_rn(sum);
+    }
+  }
+}
+
+int mma_smem_bytes(int64_t M, int64_t K, int64_t group) {
+  const int64_t T = K / 16, G = K / group, mt = std::min<int64_t>(M, kMaxM);
+  const int64_t bytes = kRows * (K / 2 + 16) + mt * (32 * ((T + 1) & ~1) + 64) + mt * (((T + 1) & ~1) + 2) * 4 +
+                        2 * kRows * G * 4 +
+                        kWarps * kMaxM * kRows * 4 + 32;
+  return int(bytes);
+}
+
+}  // namespace
+
+// The tensor-core path takes K a multiple of 16 and of the group (group a multiple of 16), 16-byte aligned rows,
+// and shapes whose staging fits two CTAs per SM; M is split into chunks of 16 rows.
+bool w4a16_mma_applies(int64_t M, int64_t N, int64_t K, int64_t group) {
+  (void)N;
+  return K % 32 == 0 && group % 16 == 0 && K / 16 >= kWarps && mma_smem_bytes(M, K, group) <= kSmemLimit;
+}
+
+int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
+              int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
+              cudaStream_t stream) {
+  MmaArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.qweight = reinterpret_cast<const uint8_t*>(qweight);
+  a.scales = static_cast<const __half*>(scales);
+  a.qzeros = reinterpret_cast<const uint32_t*>(qzeros);
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.M = int(M);
+  a.N = int(N);
+  a.K = int(K);
+  a.group = int(group);
+  a.G = int(K / group);
+  a.ZW = (a.G + 7) / 8;
+  a.T = int(K / 16);
+  a.pitch = int(K / 2 + 16);
+  a.xpitch = 32 * ((a.T + 1) & ~1) + 64;
+  a.spitch = ((a.T + 1) & ~1) + 2;
+  const int smem = mma_smem_bytes(M, K, group);
+  auto kernel = fused ? w4a16_mma_kernel<true> : w4a16_mma_kernel<false>;
+  int st = set_max_smem(reinterpret_cast<const void*>(kernel), smem);
+  if (st) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((N + kRows - 1) / kRows), unsigned((M + kMaxM - 1) / kMaxM), 1);
+  cfg.blockDim = dim3(32 * kWarps, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & BPT_FLAG_PDL) ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+  if (err != cudaSuccess) return set_error(BPT_ERR_CUDA, "w4a16 mma launch: %s", cudaGetErrorString(err));
+  return BPT_OK;
+}
+
+}  // namespace bpt

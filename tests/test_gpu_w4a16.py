@@ -68,6 +68,12 @@ def test_linear_shapes(n, k, group):
     check_linear(4, n, k, group, seed=n + 1)
 
 
+def test_m16_long_k_takes_the_cuda_core_kernel():
+    # 16 rows of x at K = 6144 do not fit the tensor-core kernel's staging: the CUDA-core kernel runs them
+    check_linear(16, 256, 6144, 128, seed=11)
+    check_linear(9, 264, 6144, 128, seed=12)
+
+
 def test_symmetric_layout_without_zero_points():
     check_linear(1, 512, 1024, 128, symmetric=True)
 
