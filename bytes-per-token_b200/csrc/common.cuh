@@ -118,6 +118,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// The same wait for a long one (a whole tile's copies): after the first test the thread sleeps `sleep_ns`
+// between tests, so waiting warps leave the issue slots to the warps that have work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
+                                                uint64_t limit_ns = 200000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0 && global_timer_ns() - start > limit_ns) {
+      record_error(kDevErrTimeout);
+      return false;
+    }
+  }
+}
+
 // The same wait, made uniform across a warp: lane 0 spins (bounded), the verdict is broadcast, and on success
 // every lane re-observes the completed phase so that each gets the barrier's acquire ordering.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 200000000ull) {

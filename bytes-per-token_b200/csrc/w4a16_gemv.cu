@@ -232,7 +232,8 @@ int w4a16_gemv(const void* x, int64_t ldx, const int32_t* qweight, const void* s
                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                cudaStream_t stream) {
   static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
-  if (!cuda_cores && w4a16_mma_applies(M, N, K, group))
+  // (it stages the scales and zero points with bulk copies: both 16-byte aligned)
+  if (!cuda_cores && w4a16_mma_applies(M, N, K, group) && aligned16(scales) && (!qzeros || aligned16(qzeros)))
     return w4a16_mma(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
   GemvArgs a;
   a.x = static_cast<const __nv_bfloat16*>(x);

@@ -38,11 +38,14 @@ struct MmaArgs {
   int pitch;   // weight row pitch in shared memory: K/2 + 16
   int xpitch;  // staged x row pitch in bytes: 32 T rounded up to 64, + 64 (rows g and g + 1 on other banks)
   int spitch;  // x step-sum row pitch in floats: T rounded up to even, + 2
+  int sbytes;  // the CTA's scales: 8 x G f16, rounded up to 16 bytes
+  int zbytes;  // the CTA's zero-point words: 8 x ZW u32 (a multiple of 16 bytes)
 };
 
+// (not volatile: a pure register operation the compiler may schedule around the loads)
 __device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -56,7 +59,7 @@ __device__ __forceinline__ uint32_t offset_codes(uint32_t w, int c) {
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 template <bool FUSED>
-__global__ void __launch_bounds__(32 * kWarps) w4a16_mma_kernel(const MmaArgs a) {
+__global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -66,48 +69,44 @@ __global__ void __launch_bounds__(32 * kWarps) w4a16_mma_kernel(const MmaArgs a)
   const int mt = min(kMaxM, a.M - m0);
   const int T = a.T;
 
-  // shared memory: weights [8][pitch] | x pairs [mt][xpitch] | x step sums [mt][spitch] f32 | scales [8][G] f32 |
-  // zeros + 128 [8][G] f32 | partials [warps][16][8] f32 | mbarrier
+  // shared memory: weights [8][pitch] | scales [8][G] f16 | zero-point words [8][ZW] | x pairs [mt][xpitch] |
+  // x step sums [mt][spitch] f32 | partials [warps][16][8] f32 | mbarrier
   uint8_t* wsm = smem;
-  uint8_t* xq = wsm + kRows * a.pitch;
+  __half* sraw = reinterpret_cast<__half*>(wsm + kRows * a.pitch);
+  uint32_t* zraw = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(sraw) + a.sbytes);
+  uint8_t* xq = reinterpret_cast<uint8_t*>(zraw) + a.zbytes;
   float* xs = reinterpret_cast<float*>(xq + mt * a.xpitch);
-  float* ssm = xs + mt * a.spitch;
-  float* zsm = ssm + kRows * a.G;
-  float* red = zsm + kRows * a.G;
+  float* red = xs + mt * a.spitch;
   uint64_t* bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(red + kWarps * kMaxM * kRows) + 15) &
                                               ~uintptr_t(15));
 
+  const bool whole = nrows == kRows;  // the last CTA may hold fewer rows: its grid comes in by plain loads
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
+  }
+  if (!whole) {
+    for (int i = tid; i < nrows * a.G; i += blockDim.x) sraw[i] = a.scales[int64_t(row0) * a.G + i];
+    if (a.qzeros)
+      for (int i = tid; i < nrows * a.ZW; i += blockDim.x) zraw[i] = a.qzeros[int64_t(row0) * a.ZW + i];
   }
   __syncthreads();
   const int row_bytes = a.K >> 1;
   if (tid == 0) {  // the weights do not depend on the previous kernel: request them before waiting on it
     const uint64_t policy = l2_policy_evict_first();
-    mbar_arrive_expect_tx(bar, uint32_t(nrows * row_bytes));
+    const bool zeros = whole && a.qzeros;
+    mbar_arrive_expect_tx(bar, uint32_t(nrows * row_bytes + (whole ? a.sbytes : 0) + (zeros ? a.zbytes : 0)));
     for (int r = 0; r < nrows; ++r)
       bulk_g2s_evict_first(wsm + r * a.pitch, a.qweight + int64_t(row0 + r) * row_bytes, row_bytes, bar, policy);
-  }
-
-  // Each warp works on k-steps [t0, t1) and stages only what that range needs: the groups' scales and zero
-  // points, then (after the previous kernel is done) x.
-  const int t0 = warp * T / kWarps, t1 = (warp + 1) * T / kWarps;
-  const int spg = a.group >> 4;  // k-steps per group (even: the group is a multiple of 32)
-  const int g0 = t0 / spg, g1 = (t1 + spg - 1) / spg;
-  for (int i = lane; i < kRows * (g1 - g0); i += 32) {
-    const int r = i / (g1 - g0), gi = g0 + i % (g1 - g0);
-    float sc = 0.f, z = 136.f;
-    if (r < nrows) {
-      sc = __half2float(a.scales[int64_t(row0 + r) * a.G + gi]);
-      if (a.qzeros) z = 128.f + float((a.qzeros[int64_t(row0 + r) * a.ZW + (gi >> 3)] >> (4 * (gi & 7))) & 15u);
-    }
-    ssm[r * a.G + gi] = sc;
-    zsm[r * a.G + gi] = z;
+    if (whole) bulk_g2s(sraw, a.scales + int64_t(row0) * a.G, a.sbytes, bar);
+    if (zeros) bulk_g2s(zraw, a.qzeros + int64_t(row0) * a.ZW, a.zbytes, bar);
   }
   pdl_launch_dependents();
   pdl_wait();  // the activations (and the output) belong to the previous kernel until here
 
+  // Each warp works on k-steps [t0, t1) (even bounds) and stages only the x that range needs.
+  const int t0 = 2 * (warp * (T / 2) / kWarps), t1 = 2 * ((warp + 1) * (T / 2) / kWarps);
+  const int spg = a.group >> 4;  // k-steps per group (even: the group is a multiple of 32)
   // x of step t, row m, lane c: the A pairs (x[16t + c], x[16t + c + 4]) and (x[16t + 8 + c], x[16t + 12 + c]),
   // stored so that a lane reads both of a step pair (t, t + 1) with one 16-byte load; and the step's sum of x.
   const int nt = t1 - t0;
@@ -134,46 +133,76 @@ __global__ void __launch_bounds__(32 * kWarps) w4a16_mma_kernel(const MmaArgs a)
   __syncwarp();
 
   float total[4] = {0.f, 0.f, 0.f, 0.f};  // D[m = g, g + 8][n = 2c, 2c + 1]
-  if (mbar_wait_warp(bar, 0)) {
+  int arrived = 0;
+  if (lane == 0) arrived = mbar_wait_sleep(bar, 0, 128u) ? 1 : 0;
+  arrived = __shfl_sync(0xffffffffu, arrived, 0);
+  if (arrived) (void)mbar_try_wait(bar, 0);  // every lane observes the completed phase (acquire)
+  if (arrived) {
     const uint8_t* wrow = wsm + g * a.pitch;
-    const bool row_a = g < mt, row_b = g + 8 < mt;
-    const uint8_t* xa = xq + g * a.xpitch + c * 16;
-    const uint8_t* xb = xq + (g + 8) * a.xpitch + c * 16;
-    const float* sxa = xs + g * a.spitch;
-    const float* sxb = xs + (g + 8) * a.spitch;
+    // Rows of D at or past mt are never stored, so lanes beyond the x rows read a valid row instead of
+    // branching: every load is unconditional.
+    const int ga = min(g, mt - 1), gb = min(g + 8, mt - 1);
+    const uint8_t* xa = xq + ga * a.xpitch + c * 16;
+    const uint8_t* xb = xq + gb * a.xpitch + c * 16;
+    const float* sxa = xs + ga * a.spitch;
+    const float* sxb = xs + gb * a.spitch;
+    const bool two = mt > 8;  // A rows g + 8 carry x (warp-uniform)
     const int n0 = 2 * c;
-    for (int grp = g0; grp < g1; ++grp) {
-      const int ta = max(t0, grp * spg), tb = min(t1, (grp + 1) * spg);
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      float sa = 0.f, sb = 0.f;  // sums of x over the steps folded here, rows g and g + 8
+    for (int grp = t0 / spg; grp * spg < t1; ++grp) {
+      const int ta = max(t0, grp * spg), tb = min(t1, (grp + 1) * spg);  // both even
+      // two independent chains: the even and the odd step of each pair
+      float ae[4] = {0.f, 0.f, 0.f, 0.f}, ao[4] = {0.f, 0.f, 0.f, 0.f};
+      float sa = 0.f, sb = 0.f;  // sums of x over the group's steps here, rows g and g + 8
       int t = ta;
-      auto one_step = [&](int tt) {
-        const uint2 wv = *reinterpret_cast<const uint2*>(wrow + 8 * tt);
-        const uint2 pa = row_a ? *reinterpret_cast<const uint2*>(xa + (tt >> 1) * 64 + (tt & 1) * 8) : make_uint2(0u, 0u);
-        const uint2 pb = row_b ? *reinterpret_cast<const uint2*>(xb + (tt >> 1) * 64 + (tt & 1) * 8) : make_uint2(0u, 0u);
-        sa += row_a ? sxa[tt] : 0.f;
-        sb += row_b ? sxb[tt] : 0.f;
-        mma_bf16(acc, pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
-      };
-      if (t & 1) one_step(t++);
-      for (; t + 2 <= tb; t += 2) {  // a step pair: one 16-byte load each of weights and x
+      for (; t + 8 <= tb; t += 8) {  // four step pairs: every load first, then the MMAs
+        uint4 wv[4], pa[4], pb[4];
+        float2 qa[4], qb[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          wv[j] = *reinterpret_cast<const uint4*>(wrow + 8 * (t + 2 * j));
+          pa[j] = *reinterpret_cast<const uint4*>(xa + ((t >> 1) + j) * 64);
+          qa[j] = *reinterpret_cast<const float2*>(sxa + t + 2 * j);
+          if (two) {
+            pb[j] = *reinterpret_cast<const uint4*>(xb + ((t >> 1) + j) * 64);
+            qb[j] = *reinterpret_cast<const float2*>(sxb + t + 2 * j);
+          } else {
+            pb[j] = make_uint4(0u, 0u, 0u, 0u);
+            qb[j] = make_float2(0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sa += qa[j].x + qa[j].y;
+          sb += qb[j].x + qb[j].y;
+          mma_bf16(ae, pa[j].x, pb[j].x, pa[j].y, pb[j].y, offset_codes(wv[j].x, c), offset_codes(wv[j].y, c));
+          mma_bf16(ao, pa[j].z, pb[j].z, pa[j].w, pb[j].w, offset_codes(wv[j].z, c), offset_codes(wv[j].w, c));
+        }
+      }
+      for (; t < tb; t += 2) {  // the group's remaining pairs (groups of fewer than 8 steps, range edges)
         const uint4 wv = *reinterpret_cast<const uint4*>(wrow + 8 * t);
-        const uint4 pa = row_a ? *reinterpret_cast<const uint4*>(xa + (t >> 1) * 64) : make_uint4(0u, 0u, 0u, 0u);
-        const uint4 pb = row_b ? *reinterpret_cast<const uint4*>(xb + (t >> 1) * 64) : make_uint4(0u, 0u, 0u, 0u);
-        const float2 qa = row_a ? *reinterpret_cast<const float2*>(sxa + t) : make_float2(0.f, 0.f);
-        const float2 qb = row_b ? *reinterpret_cast<const float2*>(sxb + t) : make_float2(0.f, 0.f);
+        const uint4 pa = *reinterpret_cast<const uint4*>(xa + (t >> 1) * 64);
+        const float2 qa = *reinterpret_cast<const float2*>(sxa + t);
+        uint4 pb = make_uint4(0u, 0u, 0u, 0u);
+        float2 qb = make_float2(0.f, 0.f);
+        if (two) {
+          pb = *reinterpret_cast<const uint4*>(xb + (t >> 1) * 64);
+          qb = *reinterpret_cast<const float2*>(sxb + t);
+        }
         sa += qa.x + qa.y;
         sb += qb.x + qb.y;
-        mma_bf16(acc, pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
-        mma_bf16(acc, pa.z, pb.z, pa.w, pb.w, offset_codes(wv.z, c), offset_codes(wv.w, c));
+        mma_bf16(ae, pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
+        mma_bf16(ao, pa.z, pb.z, pa.w, pb.w, offset_codes(wv.z, c), offset_codes(wv.w, c));
       }
-      if (t < tb) one_step(t);
-      const float s0 = ssm[n0 * a.G + grp], s1 = ssm[(n0 + 1) * a.G + grp];
-      const float z0 = zsm[n0 * a.G + grp], z1 = zsm[(n0 + 1) * a.G + grp];
-      total[0] += s0 * (acc[0] - z0 * sa);
-      total[1] += s1 * (acc[1] - z1 * sa);
-      total[2] += s0 * (acc[2] - z0 * sb);
-      total[3] += s1 * (acc[3] - z1 * sb);
+      const float s0 = __half2float(sraw[n0 * a.G + grp]), s1 = __half2float(sraw[(n0 + 1) * a.G + grp]);
+      float z0 = 136.f, z1 = 136.f;  // 128 + the zero point (8 when the layout is symmetric)
+      if (a.qzeros) {
+        z0 = 128.f + float((zraw[n0 * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u);
+        z1 = 128.f + float((zraw[(n0 + 1) * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u);
+      }
+      total[0] += s0 * ((ae[0] + ao[0]) - z0 * sa);
+      total[1] += s1 * ((ae[1] + ao[1]) - z1 * sa);
+      total[2] += s0 * ((ae[2] + ao[2]) - z0 * sb);
+      total[3] += s1 * ((ae[3] + ao[3]) - z1 * sb);
     }
   }
   float* rw = red + warp * kMaxM * kRows;
@@ -208,10 +237,10 @@ __global__ void __launch_bounds__(32 * kWarps) w4a16_mma_kernel(const MmaArgs a)
 }
 
 int mma_smem_bytes(int64_t M, int64_t K, int64_t group) {
-  const int64_t T = K / 16, G = K / group, mt = std::min<int64_t>(M, kMaxM);
-  const int64_t bytes = kRows * (K / 2 + 16) + mt * (32 * ((T + 1) & ~1) + 64) + mt * (((T + 1) & ~1) + 2) * 4 +
-                        2 * kRows * G * 4 +
-                        kWarps * kMaxM * kRows * 4 + 32;
+  const int64_t T = K / 16, G = K / group, mt = std::min<int64_t>(M, kMaxM), ZW = (G + 7) / 8;
+  const int64_t bytes = kRows * (K / 2 + 16) + ((kRows * G * 2 + 15) / 16) * 16 + kRows * ZW * 4 +
+                        mt * (32 * ((T + 1) & ~1) + 64) + mt * (((T + 1) & ~1) + 2) * 4 + kWarps * kMaxM * kRows * 4 +
+                        32;
   return int(bytes);
 }
 
@@ -221,7 +250,7 @@ int mma_smem_bytes(int64_t M, int64_t K, int64_t group) {
 // and shapes whose staging fits two CTAs per SM; M is split into chunks of 16 rows.
 bool w4a16_mma_applies(int64_t M, int64_t N, int64_t K, int64_t group) {
   (void)N;
-  return K % 32 == 0 && group % 16 == 0 && K / 16 >= kWarps && mma_smem_bytes(M, K, group) <= kSmemLimit;
+  return K % 32 == 0 && group % 32 == 0 && K / 32 >= kWarps && mma_smem_bytes(M, K, group) <= kSmemLimit;
 }
 
 int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
@@ -244,6 +273,8 @@ int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* sc
   a.T = int(K / 16);
   a.pitch = int(K / 2 + 16);
   a.xpitch = 32 * ((a.T + 1) & ~1) + 64;
+  a.sbytes = ((kRows * a.G * 2 + 15) / 16) * 16;
+  a.zbytes = kRows * a.ZW * 4;
   a.spitch = ((a.T + 1) & ~1) + 2;
   const int smem = mma_smem_bytes(M, K, group);
   auto kernel = fused ? w4a16_mma_kernel<true> : w4a16_mma_kernel<false>;
