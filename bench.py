@@ -162,10 +162,10 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         case = attn[i % ATTN_BATCHES]
         if events is not None:
             events[0].record()
-        w4a16_linear(x, qw, sc, qz, out=y)
+        w4a16_linear(x, qw, sc, qz, out=y, pdl=True)
         if events is not None:
             events[1].record()
-        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split)
+        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split, pdl=True)
         if events is not None:
             events[2].record()
 
@@ -232,8 +232,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         case.q.copy_(pin["q"][i % ATTN_BATCHES], non_blocking=True)
         case.lengths.copy_(pin["lengths"][i % ATTN_BATCHES], non_blocking=True)
         case.kv.block_table.copy_(pin["table"][i % ATTN_BATCHES], non_blocking=True)
-        w4a16_linear(x, qw, sc, qz, out=y)
-        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split)
+        w4a16_linear(x, qw, sc, qz, out=y, pdl=True)
+        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split, pdl=True)
         pin["y"].copy_(y, non_blocking=True)
         pin["out"].copy_(out, non_blocking=True)
 
@@ -295,6 +295,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             "per_rank": "one GEMV + one attention over a batch of 32 sequences per step",
             "l2": f"inputs larger than L2: {GEMV_COPIES} rotating weight copies, {ATTN_BATCHES} rotating batches/pools",
             "timing": "device lead: the host enqueues the K steps while the GPU sleeps before the region",
+            "launch": "programmatic dependent launch: each kernel's prologue overlaps the previous kernel's tail",
             "split": split,
             "parallelism": f"dp{world} (independent request batches, no collective)",
         },
