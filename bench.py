@@ -157,17 +157,17 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     gemv_bytes = workloads.w4a16_bytes(1, 6144, 2048)
     attn_bytes = [c.bytes for c in attn]
 
-    def step(i: int, events=None):
+    def gemv(i: int):
         qw, sc, qz = weights[i % GEMV_COPIES]
-        case = attn[i % ATTN_BATCHES]
-        if events is not None:
-            events[0].record()
         w4a16_linear(x, qw, sc, qz, out=y, pdl=True)
-        if events is not None:
-            events[1].record()
+
+    def attention(i: int):
+        case = attn[i % ATTN_BATCHES]
         attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split, pdl=True)
-        if events is not None:
-            events[2].record()
+
+    def step(i: int):
+        gemv(i)
+        attention(i)
 
     def barrier():
         if dist is not None:
@@ -177,8 +177,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     for i in range(max(args.warmup, 3)):
         step(i)
     barrier()
-    # host time to enqueue one step, so the timed region can start with the GPU far enough behind the host that
-    # the K steps run back to back on the device (the events then time kernels, not Python launch overhead)
+    # host time to enqueue one step, so each timed region can start with the GPU far enough behind the host that
+    # its launches run back to back on the device (the events then time kernels, not Python launch overhead)
     t0 = time.perf_counter()
     for i in range(8):
         step(i)
@@ -186,11 +186,22 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     barrier()
     clock_khz = torch.cuda.get_device_properties(device).clock_rate or 2_000_000
     lead_cycles = int(min(0.5, 2.0 * host_step_s * args.steps + 1e-3) * clock_khz * 1e3)
-
-    # device-timed region: exactly K steps, events around every kernel on the launching (current) stream
-    sampler = ClockSampler(device)
     stream = torch.cuda.current_stream(device)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+
+    def timed(fn) -> float:
+        """Device time of K launches of fn (ms): events on the launching stream around the whole sequence."""
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(lead_cycles)  # the GPU idles (outside the region) while the host enqueues the launches
+        start.record(stream)
+        for k in range(args.steps):
+            fn(k)
+        end.record(stream)
+        barrier()
+        return start.elapsed_time(end)
+
+    # device-timed regions: the step (the metric), then each kernel alone (the per-kernel rooflines)
+    sampler = ClockSampler(device)
     with sampler:
         soak_end = time.perf_counter() + 0.3  # the sampler needs a few hundred ms of the same load around the region
         i = 0
@@ -199,17 +210,11 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             i += 1
             if i % 64 == 0:
                 torch.cuda.synchronize(device)
-        barrier()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda._sleep(lead_cycles)  # the GPU idles (outside the region) while the host enqueues the steps
-        start.record(stream)
-        for k in range(args.steps):
-            step(k, ev[k])
-        end.record(stream)
-        barrier()
-    total_ms = start.elapsed_time(end)
-    gemv_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    attn_ms = [e[1].elapsed_time(e[2]) for e in ev]
+        total_ms = timed(step)
+        attn_total_ms = timed(attention)
+        gemv_total_ms = timed(gemv)
+    gemv_ms = [gemv_total_ms / args.steps]
+    attn_ms = [attn_total_ms / args.steps]
     my_bytes = sum(gemv_bytes + attn_bytes[k % ATTN_BATCHES] for k in range(args.steps))
 
     # end to end: the public API with host buffers, the step's inputs H2D and results D2H inside the region
@@ -320,6 +325,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e_max / args.steps, 5)},
         "gpu_launches": 2 * args.steps,
+        "gpu_launches_note": "the step region; the per-kernel regions launch K more of each kernel",
         "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": reasons,
                    "samples": clocks["samples"], "window": "0.3 s soak of the same step + the timed region"},
     }
