@@ -227,11 +227,18 @@ bool w4a16_mma_applies(int64_t M, int64_t N, int64_t K, int64_t group);
 int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
               int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
 
-// Small M: the tensor-core kernel (w4a16_mma.cu) where its staging fits, the CUDA-core kernel below otherwise.
+bool w4a16_gemm_applies(int64_t M, int64_t N, int64_t K, int64_t group);
+int w4a16_gemm(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
+               int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
+
+// M >= 32: the tiled tensor-core GEMM (w4a16_gemm.cu). Small M: the tensor-core GEMV (w4a16_mma.cu) where its
+// staging fits, the CUDA-core kernel below otherwise.
 int w4a16_gemv(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                cudaStream_t stream) {
   static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
+  if (!cuda_cores && w4a16_gemm_applies(M, N, K, group))
+    return w4a16_gemm(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
   // (it stages the scales and zero points with bulk copies: both 16-byte aligned)
   if (!cuda_cores && w4a16_mma_applies(M, N, K, group) && aligned16(scales) && (!qzeros || aligned16(qzeros)))
     return w4a16_mma(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);

@@ -1,0 +1,104 @@
+"""The Qwen3 decode step (config 5's caller of the hot path) against the oracle, layer by layer.
+
+Each decoder layer is recomputed from the same input hidden state by the reference's arithmetic
+(engine/model.py) with the oracle's dequantized W4A16 weights and its paged attention over the same pool; the
+KV codes the step writes must equal the oracle's FP8 store bit for bit.
+"""
+
+import math
+
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import kv_formats as okv
+from oracle import w4a16 as ow4
+
+pytestmark = pytest.mark.gpu
+
+
+def dequant(t):
+    qweight, scales, qzeros = [x.cpu() for x in t]
+    n, k = qweight.shape[0], qweight.shape[1] * 8
+    g = k // scales.shape[1]
+    codes = ow4.unpack_nibbles_int32(qweight, k)
+    zeros = ow4.unpack_nibbles_int32(qzeros, k // g)
+    return ow4.dequantize_w4a16(codes, scales, zeros, g)
+
+
+def linear(x, w):  # the reference's fp32 linear over the dequantized weight, rounded once to bf16
+    return (x.float() @ w.T).to(torch.bfloat16)
+
+
+def reference_layer(dec, layer, h, cos, sin, lengths_after, kpool, vpool):
+    """engine/model.py's DecoderLayer.forward for one token, on the CPU, over the given pools."""
+    from bpt_b200.decode import rms_norm, rope_apply
+
+    d = dec.dims
+    b = h.shape[0]
+    qd, kd = d.q_heads * d.head_dim, d.kv_heads * d.head_dim
+    x = rms_norm(h, layer.input_norm.cpu(), d.eps)
+    qkv = linear(x, dequant(layer.qkv))
+    q = rms_norm(qkv[:, :qd].view(b, d.q_heads, d.head_dim), layer.q_norm.cpu(), d.eps)
+    k = rms_norm(qkv[:, qd : qd + kd].view(b, d.kv_heads, d.head_dim), layer.k_norm.cpu(), d.eps)
+    v = qkv[:, qd + kd :].view(b, d.kv_heads, d.head_dim)
+    q, k = rope_apply(q, cos, sin), rope_apply(k, cos, sin)
+    kv = okv.PagedKV("fp8", kpool, vpool, layer.kv.k_scale, layer.kv.v_scale, dec.block_table.cpu(), 16)
+    attn = oatt.paged_attend(q.float(), kv, lengths_after, 1.0 / math.sqrt(d.head_dim)).to(torch.bfloat16)
+    h = h + linear(attn.reshape(b, qd), dequant(layer.o))
+    x = rms_norm(h, layer.post_norm.cpu(), d.eps)
+    gu = dequant(layer.gate_up)
+    g, u = (x.float() @ gu[0::2].T), (x.float() @ gu[1::2].T)
+    act = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)
+    return h + linear(act, dequant(layer.down)), k, v
+
+
+def test_decode_step_layers_match_reference():
+    from bpt_b200.decode import Qwen3Decoder, Qwen3Dims, rope_cos_sin
+
+    dims = Qwen3Dims(layers=2, intermediate=1024, vocab=512)
+    lengths = torch.tensor([40, 17, 100, 64])
+    dec = Qwen3Decoder(dims, lengths, seed=3, capacity=8)
+    dec.tokens.copy_(torch.tensor([1, 7, 300, 42]))
+    b = dec.batch
+    pos = dec.lengths.to(torch.int64)
+    cos, sin = rope_cos_sin(pos, dims.head_dim, dims.rope_theta, torch.bfloat16)
+    write_blocks = torch.gather(dec.block_table, 1, (pos // 16)[:, None]).to(torch.int32)
+    write_offsets = (pos % 16).to(torch.int32)[:, None]
+    lengths_after = dec.lengths + 1
+    h = dec.embed[dec.tokens]
+    for layer in dec.layers:
+        before_k, before_v = layer.kv.k_pool.cpu(), layer.kv.v_pool.cpu()
+        got = dec.layer_forward(layer, h, cos, sin, write_blocks, write_offsets, lengths_after)
+        torch.cuda.synchronize()
+        kpool, vpool = layer.kv.k_pool.cpu(), layer.kv.v_pool.cpu()
+        want, k, v = reference_layer(dec, layer, h.cpu(), cos.cpu(), sin.cpu(), lengths_after.cpu(), kpool, vpool)
+        # the step wrote exactly this token's K and V codes, and nothing else
+        wb, wo = write_blocks.cpu()[:, 0], write_offsets.cpu()[:, 0]
+        for i in range(b):
+            assert torch.equal(kpool[wb[i], wo[i]], okv.fp8_store(k[i].float(), float(layer.kv.k_scale)))
+            assert torch.equal(vpool[wb[i], wo[i]], okv.fp8_store(v[i].float(), float(layer.kv.v_scale)))
+            before_k[wb[i], wo[i]] = kpool[wb[i], wo[i]]
+            before_v[wb[i], wo[i]] = vpool[wb[i], wo[i]]
+        assert torch.equal(before_k, kpool) and torch.equal(before_v, vpool)
+        err = (got.cpu().float() - want.float()).norm() / want.float().norm()
+        assert err < 2e-2, err
+        h = got
+
+
+def test_decode_step_graph_replay_equals_eager():
+    from bpt_b200.decode import Qwen3Decoder, Qwen3Dims
+
+    dims = Qwen3Dims(layers=2, intermediate=1024, vocab=512)
+    lengths = torch.tensor([33, 16, 150, 1])
+    eager = Qwen3Decoder(dims, lengths, seed=5, capacity=8)
+    graphed = Qwen3Decoder(dims, lengths, seed=5, capacity=8)
+    graphed.capture()  # one eager step inside, then the capture
+    eager.step()
+    for _ in range(3):
+        eager.step()
+        graphed.step()
+    torch.cuda.synchronize()
+    assert torch.equal(eager.lengths, graphed.lengths)
+    assert torch.equal(eager.tokens, graphed.tokens)
+    torch.testing.assert_close(eager.hidden.float(), graphed.hidden.float(), atol=0, rtol=0)

@@ -68,6 +68,32 @@ def test_linear_shapes(n, k, group):
     check_linear(4, n, k, group, seed=n + 1)
 
 
+@pytest.mark.parametrize("m", [32, 33, 64, 100, 256])
+def test_gemm_m_at_least_32(m):
+    # the tiled tensor-core GEMM: M tiles of 64 (ragged last tile), N tiles of 32 (ragged: 1000, 2056)
+    check_linear(m, 1000, 2048, 128, seed=m)
+    check_linear(m, 2056, 6144, 128, seed=m + 1)
+
+
+def test_gemm_group_64_and_symmetric():
+    check_linear(64, 512, 1024, 64, seed=21)
+    check_linear(48, 512, 1024, 128, seed=22, symmetric=True)
+
+
+def test_gemm_gate_up_silu():
+    from bpt_b200.kernels.w4a16 import interleave_rows, quantize_w4a16, w4a16_gate_up_silu
+
+    i, k = 1536, 2048
+    gate, up = dense(i, k, 13), dense(i, k, 14)
+    x = acts(64, k, 15)
+    qg, qu = quantize_w4a16(gate.cuda()), quantize_w4a16(up.cuda())
+    fused = [interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)]
+    got = w4a16_gate_up_silu(x.cuda(), *fused)
+    g = ow4.w4a16_linear(x, *[t.cpu() for t in qg], 128).float()
+    u = ow4.w4a16_linear(x, *[t.cpu() for t in qu], 128).float()
+    torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
+
+
 def test_m16_long_k_takes_the_cuda_core_kernel():
     # 16 rows of x at K = 6144 do not fit the tensor-core kernel's staging: the CUDA-core kernel runs them
     check_linear(16, 256, 6144, 128, seed=11)
