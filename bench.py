@@ -124,6 +124,33 @@ class ClockSampler:
         return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
 
 
+# ---- ranks --------------------------------------------------------------------------------------------------------
+
+
+def gather_ranks(local: dict, dist) -> list[dict]:
+    """Every rank's measurement dict, in rank order, on every rank (one all_gather_object; None: one process)."""
+    if dist is None:
+        return [local]
+    gathered = [None] * dist.get_world_size()
+    dist.all_gather_object(gathered, local)
+    return gathered
+
+
+def combine_ranks(gathered: list[dict]) -> dict:
+    """Whole-job figures: the slowest rank's device time for each timed region, the sum of every rank's bytes
+    (and decode tokens). Each rank runs the same number of steps on its own batch (weak scaling)."""
+    out = {
+        "total_ms": max(g["total_ms"] for g in gathered),
+        "e2e_ms": max(g["e2e_ms"] for g in gathered),
+        "bytes": sum(g["bytes"] for g in gathered),
+    }
+    if all("decode_ms" in g for g in gathered):
+        out["decode_ms"] = max(g["decode_ms"] for g in gathered)
+        out["decode_tokens"] = sum(g["decode_tokens"] for g in gathered)
+        out["decode_bytes"] = sum(g["decode_bytes"] for g in gathered)
+    return out
+
+
 # ---- our arm ------------------------------------------------------------------------------------------------------
 
 
@@ -261,17 +288,16 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "attn_ms": attn_ms,
         "clocks": sampler.summary(),
     }
-    if dist is not None:
-        gathered = [None] * world
-        dist.all_gather_object(gathered, local)
-    else:
-        gathered = [local]
+    del weights, attn, pin
+    torch.cuda.empty_cache()
+    if not args.no_decode:
+        local.update(decode_step_timing(args, rank, device, barrier))
+    gathered = gather_ranks(local, dist)
     if rank != 0:
         return None
 
-    t_max = max(g["total_ms"] for g in gathered)
-    e_max = max(g["e2e_ms"] for g in gathered)
-    all_bytes = sum(g["bytes"] for g in gathered)
+    whole = combine_ranks(gathered)
+    t_max, e_max, all_bytes = whole["total_ms"], whole["e2e_ms"], whole["bytes"]
     gbs = all_bytes / (t_max * 1e-3) / 1e9
     e2e_gbs = all_bytes / (e_max * 1e-3) / 1e9
     peak, peak_kind = measured_peaks()
@@ -329,9 +355,52 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": reasons,
                    "samples": clocks["samples"], "window": "0.3 s soak of the same step + the timed region"},
     }
+    if "decode_ms" in whole:
+        ms = whole["decode_ms"] / args.decode_steps
+        line["decode_step"] = {
+            "config": "config 5: Qwen3-1.7B decode step (28 layers, hidden 2048, intermediate 6144, 16 Q / 8 KV heads, "
+                      "head_dim 128), random INT4 g128 weights + FP8 KV, batch 64 per GPU, contexts U[1024,8192]; "
+                      "one CUDA graph per step; independent batches per rank, no collective",
+            "tokens_per_s": round(whole["decode_tokens"] / (whole["decode_ms"] * 1e-3), 1),
+            "ms_per_step": round(ms, 4),
+            "gbs": round(whole["decode_bytes"] / (whole["decode_ms"] * 1e-3) / 1e9, 1),
+            "bytes_per_step_per_gpu": gathered[0]["decode_bytes"] // args.decode_steps,
+            "steps": args.decode_steps,
+            "scaling": "weak",
+        }
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(sample_seqs=4)
     return line
+
+
+def decode_step_timing(args, rank: int, device: torch.device, barrier) -> dict:
+    """Config 5 on this rank: its own batch of 64 sequences (seeded by the rank), one graph-captured step per
+    launch; device time of `decode_steps` steps with the GPU leading as for the other regions."""
+    from bpt_b200.decode import Qwen3Decoder, Qwen3Dims
+
+    g = torch.Generator().manual_seed(1000 + rank)
+    lengths = torch.randint(1024, 8193, (64,), generator=g)
+    dec = Qwen3Decoder(Qwen3Dims(), lengths, device=device, seed=rank, capacity=args.decode_steps + 8)
+    dec.capture()
+    for _ in range(3):
+        dec.step()
+    barrier()
+    kv0 = dec.kv_bytes_per_step()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(int(2e6))
+    start.record()
+    for _ in range(args.decode_steps):
+        dec.step()
+    end.record()
+    barrier()
+    ms = start.elapsed_time(end)
+    d = dec.dims
+    grow = d.layers * dec.batch * 2 * d.kv_heads * d.head_dim  # one more token per sequence each step
+    per_step = kv0 + (args.decode_steps - 1) * grow // 2 + dec.weight_bytes_per_step()  # mean KV read + weights
+    dec.graph = None
+    del dec
+    torch.cuda.empty_cache()
+    return {"decode_ms": ms, "decode_tokens": 64 * args.decode_steps, "decode_bytes": per_step * args.decode_steps}
 
 
 # ---- the CPU baseline: the reference path restated (oracle port) on the host cores ------------------------------
@@ -420,8 +489,10 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--decode-steps", type=int, default=20, help="config-5 decode steps timed (0: skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    args.no_decode = args.decode_steps <= 0
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
