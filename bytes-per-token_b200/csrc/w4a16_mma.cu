@@ -1,9 +1,9 @@
 // W4A16 linear for small M on the tensor cores: y[M, N] = x[M, K] . (scale * (q - zero))^T, M <= 16.
 //
-// One CTA owns 8 weight rows (the MMA's N) and all of K; its four warps split K. The CTA's rows reach shared
-// memory with one bulk copy per row (TMA engine) to a padded pitch, so the lanes' 8-byte reads of the 8 rows
-// fall on different banks. A grid of ceil(N / 8) CTAs (768 for N = 6144) is resident at once, so every row of
-// the matrix is requested at the start and the kernel streams at the rate HBM delivers.
+// One CTA owns 8 weight rows (one MMA N tile; M <= 8) or 16 (two tiles sharing every x fragment; M up to 16) and
+// all of K; its four warps split K. The CTA's rows reach shared memory with one bulk copy per row (TMA engine)
+// to a padded pitch, so the lanes' 16-byte reads of 8 rows fall on different banks. The whole grid (768 CTAs for
+// N = 6144 at M = 1) is resident at once, so every row of the matrix is requested at the start.
 //
 // mma.sync m16n8k16 bf16 -> fp32, per 16 inputs of K (k-step t):
 //   B[k][n] = 128 + q[n][k]: lane (g, c) turns the two int32 words of row n = g that hold inputs 16t .. 16t+15 into
@@ -20,7 +20,7 @@
 namespace bpt {
 namespace {
 
-constexpr int kRows = 8;    // weight rows per CTA
+constexpr int kMaxRows = 16;  // weight rows per CTA: 8 (one MMA N tile) for M <= 8, 16 (two) above
 constexpr int kWarps = 4;   // K split
 constexpr int kMaxM = 16;   // x rows per launch (A has 16 rows)
 constexpr int kSmemLimit = 110 * 1024;  // two CTAs per SM at least
@@ -58,8 +58,9 @@ __device__ __forceinline__ uint32_t offset_codes(uint32_t w, int c) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
-template <bool FUSED>
-__global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs a) {
+template <bool FUSED, int kRows>
+__global__ void __launch_bounds__(32 * kWarps, kRows == 8 ? 6 : 4) w4a16_mma_kernel(const MmaArgs a) {
+  constexpr int kTiles = kRows / 8;  // 8-row MMA N tiles
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -132,13 +133,17 @@ __global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs
   }
   __syncwarp();
 
-  float total[4] = {0.f, 0.f, 0.f, 0.f};  // D[m = g, g + 8][n = 2c, 2c + 1]
+  float total[kTiles][4];  // tile nt: D[m = g, g + 8][n = 8 nt + 2c, 8 nt + 2c + 1]
+#pragma unroll
+  for (int nt = 0; nt < kTiles; ++nt) total[nt][0] = total[nt][1] = total[nt][2] = total[nt][3] = 0.f;
   int arrived = 0;
   if (lane == 0) arrived = mbar_wait_sleep(bar, 0, 128u) ? 1 : 0;
   arrived = __shfl_sync(0xffffffffu, arrived, 0);
   if (arrived) (void)mbar_try_wait(bar, 0);  // every lane observes the completed phase (acquire)
   if (arrived) {
-    const uint8_t* wrow = wsm + g * a.pitch;
+    const uint8_t* wrow[kTiles];
+#pragma unroll
+    for (int nt = 0; nt < kTiles; ++nt) wrow[nt] = wsm + (8 * nt + g) * a.pitch;
     // Rows of D at or past mt are never stored, so lanes beyond the x rows read a valid row instead of
     // branching: every load is unconditional.
     const int ga = min(g, mt - 1), gb = min(g + 8, mt - 1);
@@ -147,19 +152,23 @@ __global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs
     const float* sxa = xs + ga * a.spitch;
     const float* sxb = xs + gb * a.spitch;
     const bool two = mt > 8;  // A rows g + 8 carry x (warp-uniform)
-    const int n0 = 2 * c;
     for (int grp = t0 / spg; grp * spg < t1; ++grp) {
       const int ta = max(t0, grp * spg), tb = min(t1, (grp + 1) * spg);  // both even
-      // two independent chains: the even and the odd step of each pair
-      float ae[4] = {0.f, 0.f, 0.f, 0.f}, ao[4] = {0.f, 0.f, 0.f, 0.f};
+      // per tile two independent chains: the even and the odd step of each pair
+      float ae[kTiles][4], ao[kTiles][4];
+#pragma unroll
+      for (int nt = 0; nt < kTiles; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ae[nt][e] = ao[nt][e] = 0.f;
       float sa = 0.f, sb = 0.f;  // sums of x over the group's steps here, rows g and g + 8
       int t = ta;
       for (; t + 8 <= tb; t += 8) {  // four step pairs: every load first, then the MMAs
-        uint4 wv[4], pa[4], pb[4];
+        uint4 wv[4][kTiles], pa[4], pb[4];
         float2 qa[4], qb[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          wv[j] = *reinterpret_cast<const uint4*>(wrow + 8 * (t + 2 * j));
+#pragma unroll
+          for (int nt = 0; nt < kTiles; ++nt) wv[j][nt] = *reinterpret_cast<const uint4*>(wrow[nt] + 8 * (t + 2 * j));
           pa[j] = *reinterpret_cast<const uint4*>(xa + ((t >> 1) + j) * 64);
           qa[j] = *reinterpret_cast<const float2*>(sxa + t + 2 * j);
           if (two) {
@@ -174,12 +183,14 @@ __global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs
         for (int j = 0; j < 4; ++j) {
           sa += qa[j].x + qa[j].y;
           sb += qb[j].x + qb[j].y;
-          mma_bf16(ae, pa[j].x, pb[j].x, pa[j].y, pb[j].y, offset_codes(wv[j].x, c), offset_codes(wv[j].y, c));
-          mma_bf16(ao, pa[j].z, pb[j].z, pa[j].w, pb[j].w, offset_codes(wv[j].z, c), offset_codes(wv[j].w, c));
+#pragma unroll
+          for (int nt = 0; nt < kTiles; ++nt) {
+            mma_bf16(ae[nt], pa[j].x, pb[j].x, pa[j].y, pb[j].y, offset_codes(wv[j][nt].x, c), offset_codes(wv[j][nt].y, c));
+            mma_bf16(ao[nt], pa[j].z, pb[j].z, pa[j].w, pb[j].w, offset_codes(wv[j][nt].z, c), offset_codes(wv[j][nt].w, c));
+          }
         }
       }
       for (; t < tb; t += 2) {  // the group's remaining pairs (groups of fewer than 8 steps, range edges)
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + 8 * t);
         const uint4 pa = *reinterpret_cast<const uint4*>(xa + (t >> 1) * 64);
         const float2 qa = *reinterpret_cast<const float2*>(sxa + t);
         uint4 pb = make_uint4(0u, 0u, 0u, 0u);
@@ -190,26 +201,37 @@ __global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs
         }
         sa += qa.x + qa.y;
         sb += qb.x + qb.y;
-        mma_bf16(ae, pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
-        mma_bf16(ao, pa.z, pb.z, pa.w, pb.w, offset_codes(wv.z, c), offset_codes(wv.w, c));
+#pragma unroll
+        for (int nt = 0; nt < kTiles; ++nt) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(wrow[nt] + 8 * t);
+          mma_bf16(ae[nt], pa.x, pb.x, pa.y, pb.y, offset_codes(wv.x, c), offset_codes(wv.y, c));
+          mma_bf16(ao[nt], pa.z, pb.z, pa.w, pb.w, offset_codes(wv.z, c), offset_codes(wv.w, c));
+        }
       }
-      const float s0 = __half2float(sraw[n0 * a.G + grp]), s1 = __half2float(sraw[(n0 + 1) * a.G + grp]);
-      float z0 = 136.f, z1 = 136.f;  // 128 + the zero point (8 when the layout is symmetric)
-      if (a.qzeros) {
-        z0 = 128.f + float((zraw[n0 * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u);
-        z1 = 128.f + float((zraw[(n0 + 1) * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u);
+#pragma unroll
+      for (int nt = 0; nt < kTiles; ++nt) {
+        const int n0 = 8 * nt + 2 * c;
+        const float s0 = __half2float(sraw[n0 * a.G + grp]), s1 = __half2float(sraw[(n0 + 1) * a.G + grp]);
+        float z0 = 136.f, z1 = 136.f;  // 128 + the zero point (8 when the layout is symmetric)
+        if (a.qzeros) {
+          z0 = 128.f + float((zraw[n0 * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u);
+          z1 = 128.f + float((zraw[(n0 + 1) * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u);
+        }
+        total[nt][0] += s0 * ((ae[nt][0] + ao[nt][0]) - z0 * sa);
+        total[nt][1] += s1 * ((ae[nt][1] + ao[nt][1]) - z1 * sa);
+        total[nt][2] += s0 * ((ae[nt][2] + ao[nt][2]) - z0 * sb);
+        total[nt][3] += s1 * ((ae[nt][3] + ao[nt][3]) - z1 * sb);
       }
-      total[0] += s0 * ((ae[0] + ao[0]) - z0 * sa);
-      total[1] += s1 * ((ae[1] + ao[1]) - z1 * sa);
-      total[2] += s0 * ((ae[2] + ao[2]) - z0 * sb);
-      total[3] += s1 * ((ae[3] + ao[3]) - z1 * sb);
     }
   }
   float* rw = red + warp * kMaxM * kRows;
-  rw[g * kRows + 2 * c] = total[0];
-  rw[g * kRows + 2 * c + 1] = total[1];
-  rw[(g + 8) * kRows + 2 * c] = total[2];
-  rw[(g + 8) * kRows + 2 * c + 1] = total[3];
+#pragma unroll
+  for (int nt = 0; nt < kTiles; ++nt) {
+    rw[g * kRows + 8 * nt + 2 * c] = total[nt][0];
+    rw[g * kRows + 8 * nt + 2 * c + 1] = total[nt][1];
+    rw[(g + 8) * kRows + 8 * nt + 2 * c] = total[nt][2];
+    rw[(g + 8) * kRows + 8 * nt + 2 * c + 1] = total[nt][3];
+  }
   __syncthreads();
   if (tid == 0) (void)mbar_wait(bar, 0, 50000000ull);  // every copy has landed before the CTA exits (bounded)
   if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
@@ -236,8 +258,11 @@ __global__ void __launch_bounds__(32 * kWarps, 6) w4a16_mma_kernel(const MmaArgs
   }
 }
 
+int mma_rows(int64_t M) { return M <= 8 ? 8 : 16; }
+
 int mma_smem_bytes(int64_t M, int64_t K, int64_t group) {
   const int64_t T = K / 16, G = K / group, mt = std::min<int64_t>(M, kMaxM), ZW = (G + 7) / 8;
+  const int64_t kRows = mma_rows(M);
   const int64_t bytes = kRows * (K / 2 + 16) + ((kRows * G * 2 + 15) / 16) * 16 + kRows * ZW * 4 +
                         mt * (32 * ((T + 1) & ~1) + 64) + mt * (((T + 1) & ~1) + 2) * 4 + kWarps * kMaxM * kRows * 4 +
                         32;
@@ -273,15 +298,17 @@ int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* sc
   a.T = int(K / 16);
   a.pitch = int(K / 2 + 16);
   a.xpitch = 32 * ((a.T + 1) & ~1) + 64;
-  a.sbytes = ((kRows * a.G * 2 + 15) / 16) * 16;
-  a.zbytes = kRows * a.ZW * 4;
+  const int rows = mma_rows(M);
+  a.sbytes = ((rows * a.G * 2 + 15) / 16) * 16;
+  a.zbytes = rows * a.ZW * 4;
   a.spitch = ((a.T + 1) & ~1) + 2;
   const int smem = mma_smem_bytes(M, K, group);
-  auto kernel = fused ? w4a16_mma_kernel<true> : w4a16_mma_kernel<false>;
+  auto kernel = rows == 8 ? (fused ? w4a16_mma_kernel<true, 8> : w4a16_mma_kernel<false, 8>)
+                          : (fused ? w4a16_mma_kernel<true, 16> : w4a16_mma_kernel<false, 16>);
   int st = set_max_smem(reinterpret_cast<const void*>(kernel), smem);
   if (st) return st;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned((N + kRows - 1) / kRows), unsigned((M + kMaxM - 1) / kMaxM), 1);
+  cfg.gridDim = dim3(unsigned((N + rows - 1) / rows), unsigned((M + kMaxM - 1) / kMaxM), 1);
   cfg.blockDim = dim3(32 * kWarps, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
