@@ -3,9 +3,13 @@
     python -m bpt_b200.profile_case attention-config2 [--launches 4]
     python -m bpt_b200.profile_case attention-config3
     python -m bpt_b200.profile_case gemv-config1
+    python -m bpt_b200.profile_case w4a16-sweep
 
-Each case builds its seeded synthetic inputs once, then launches the kernel `--launches` times back to back and
-prints the mean device time per launch (CUDA events; not a benchmark number under a profiler).
+Each kernel case builds its seeded synthetic inputs once, then launches the kernel `--launches` times back to
+back and prints the mean device time per launch (CUDA events; not a benchmark number under a profiler).
+`w4a16-sweep` is config 4: every Qwen3-1.7B decoder linear at M in {1, 4, 16, 64, 256}, each timed by replaying
+a CUDA graph of calls that rotate over enough weight copies to exceed L2 (so every call reads HBM), with
+programmatic dependent launch; it prints a markdown table of us per call, GB/s (algorithmic bytes) and TFLOP/s.
 """
 
 from __future__ import annotations
@@ -16,6 +20,7 @@ import math
 import torch
 
 from . import workloads
+from .workloads import w4a16_bytes
 from .kernels.kv_attention import attend, attend_workspace
 from .kernels.w4a16 import quantize_w4a16, w4a16_linear
 
@@ -39,6 +44,63 @@ def _gemv(launches: int) -> float:
     return _time(lambda: w4a16_linear(x, qw, sc, qz, out=y), launches)
 
 
+SWEEP_SHAPES = [("q_proj / o_proj", 2048, 2048), ("k_proj / v_proj", 1024, 2048), ("gate_up (fused, SiLU)", 12288, 2048),
+                ("down_proj", 2048, 6144)]
+SWEEP_M = [1, 4, 16, 64, 256]
+
+
+def _sweep() -> None:
+    from .kernels.w4a16 import w4a16_gate_up_silu
+
+    peak = _peak_gbs()
+    print("| linear | N x K | M | us per call | GB/s | of HBM peak | TFLOP/s |")
+    print("|---|---|---|---|---|---|---|")
+    for name, n, k in SWEEP_SHAPES:
+        copies = max(2, min(40, int(300e6 // (n * k // 2))))
+        g = torch.Generator(device="cuda").manual_seed(n + k)
+        ws = [quantize_w4a16(torch.randn(n, k, generator=g, device="cuda") * 0.02, 128) for _ in range(copies)]
+        fused = name.startswith("gate_up")
+        for m in SWEEP_M:
+            x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+            y = torch.empty(m, n // 2 if fused else n, dtype=torch.bfloat16, device="cuda")
+            fn = w4a16_gate_up_silu if fused else w4a16_linear
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                for w in ws:
+                    fn(x, *w, out=y, pdl=True)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for w in ws:
+                    fn(x, *w, out=y, pdl=True)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 10
+            start.record()
+            for _ in range(reps):
+                graph.replay()
+            end.record()
+            torch.cuda.synchronize()
+            us = start.elapsed_time(end) * 1e3 / (reps * copies)
+            nbytes = w4a16_bytes(m, n, k) - (2 * m * n // 2 if fused else 0)
+            gbs = nbytes / us / 1e3
+            print(f"| {name} | {n} x {k} | {m} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} | {2 * m * n * k / us / 1e6:.1f} |",
+                  flush=True)
+            del graph
+        del ws
+        torch.cuda.empty_cache()
+
+
+def _peak_gbs() -> float:
+    import json
+    from pathlib import Path
+
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    return float(json.loads(path.read_text())["hbm_gbs"]) if path.exists() else 6650.0
+
+
 def _time(fn, launches: int) -> float:
     fn()
     torch.cuda.synchronize()
@@ -53,9 +115,12 @@ def _time(fn, launches: int) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("case", choices=["attention-config2", "attention-config3", "gemv-config1"])
+    ap.add_argument("case", choices=["attention-config2", "attention-config3", "gemv-config1", "w4a16-sweep"])
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
+    if args.case == "w4a16-sweep":
+        _sweep()
+        return
     if args.case == "gemv-config1":
         us = _gemv(args.launches)
     else:

@@ -15,9 +15,12 @@
 //   sum_k x_k s (q_k - z) = s (sum_k x_k (128 + q_k) - (128 + z) sum_k x_k),
 // with the MMA accumulating the first sum over a group's steps and the second coming from per-step sums of x.
 // The warps' partial sums meet in shared memory in a fixed order: results are deterministic.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace bpt {
+namespace cg = cooperative_groups;
 namespace {
 
 constexpr int kMaxRows = 16;  // weight rows per CTA: 8 (one MMA N tile) for M <= 8, 16 (two) above
@@ -34,8 +37,10 @@ struct MmaArgs {
   __nv_bfloat16* y;
   int64_t ldy;
   int M, N, K, group, G, ZW;
-  int T;       // k-steps: K / 16
-  int pitch;   // weight row pitch in shared memory: K/2 + 16
+  int ks;      // CTAs splitting K: one thread-block cluster per row tile
+  int Kc;      // inputs per CTA: K / ks
+  int T;       // the CTA's k-steps: Kc / 16
+  int pitch;   // weight row pitch in shared memory: Kc/2 + 16
   int xpitch;  // staged x row pitch in bytes: 32 T rounded up to 64, + 64 (rows g and g + 1 on other banks)
   int spitch;  // x step-sum row pitch in floats: T rounded up to even, + 2
   int sbytes;  // the CTA's scales: 8 x G f16, rounded up to 16 bytes
@@ -64,7 +69,9 @@ __global__ void __launch_bounds__(32 * kWarps, kRows == 8 ? 6 : 4) w4a16_mma_ker
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int row0 = blockIdx.x * kRows;
+  const int kr = blockIdx.x % a.ks;                     // this CTA's K slice (its rank in the cluster)
+  const int row0 = (blockIdx.x / a.ks) * kRows;
+  const int toff = kr * a.T;                            // the slice's first k-step
   const int nrows = min(kRows, a.N - row0);
   const int m0 = blockIdx.y * kMaxM;
   const int mt = min(kMaxM, a.M - m0);
@@ -92,13 +99,14 @@ __global__ void __launch_bounds__(32 * kWarps, kRows == 8 ? 6 : 4) w4a16_mma_ker
       for (int i = tid; i < nrows * a.ZW; i += blockDim.x) zraw[i] = a.qzeros[int64_t(row0) * a.ZW + i];
   }
   __syncthreads();
-  const int row_bytes = a.K >> 1;
+  const int row_bytes = a.Kc >> 1;
   if (tid == 0) {  // the weights do not depend on the previous kernel: request them before waiting on it
     const uint64_t policy = l2_policy_evict_first();
     const bool zeros = whole && a.qzeros;
     mbar_arrive_expect_tx(bar, uint32_t(nrows * row_bytes + (whole ? a.sbytes : 0) + (zeros ? a.zbytes : 0)));
     for (int r = 0; r < nrows; ++r)
-      bulk_g2s_evict_first(wsm + r * a.pitch, a.qweight + int64_t(row0 + r) * row_bytes, row_bytes, bar, policy);
+      bulk_g2s_evict_first(wsm + r * a.pitch, a.qweight + int64_t(row0 + r) * (a.K >> 1) + int64_t(kr) * row_bytes,
+                           row_bytes, bar, policy);
     if (whole) bulk_g2s(sraw, a.scales + int64_t(row0) * a.G, a.sbytes, bar);
     if (zeros) bulk_g2s(zraw, a.qzeros + int64_t(row0) * a.ZW, a.zbytes, bar);
   }
@@ -113,7 +121,7 @@ __global__ void __launch_bounds__(32 * kWarps, kRows == 8 ? 6 : 4) w4a16_mma_ker
   const int nt = t1 - t0;
   for (int i = lane; i < mt * nt; i += 32) {
     const int m = i / nt, t = t0 + i % nt;
-    const uint4* src = reinterpret_cast<const uint4*>(a.x + int64_t(m0 + m) * a.ldx + 16 * t);
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + int64_t(m0 + m) * a.ldx + 16 * (toff + t));
     const uint4 u0 = src[0], u1 = src[1];  // inputs 0..7 and 8..15 of the step, as bf16 pairs
     const uint32_t lo[4] = {u0.x, u0.y, u0.z, u0.w}, hi[4] = {u1.x, u1.y, u1.z, u1.w};
     float sum = 0.f;
@@ -152,8 +160,8 @@ __global__ void __launch_bounds__(32 * kWarps, kRows == 8 ? 6 : 4) w4a16_mma_ker
     const float* sxa = xs + ga * a.spitch;
     const float* sxb = xs + gb * a.spitch;
     const bool two = mt > 8;  // A rows g + 8 carry x (warp-uniform)
-    for (int grp = t0 / spg; grp * spg < t1; ++grp) {
-      const int ta = max(t0, grp * spg), tb = min(t1, (grp + 1) * spg);  // both even
+    for (int grp = (toff + t0) / spg; grp * spg < toff + t1; ++grp) {  // groups numbered over all of K
+      const int ta = max(t0, grp * spg - toff), tb = min(t1, (grp + 1) * spg - toff);  // local, both even
       // per tile two independent chains: the even and the odd step of each pair
       float ae[kTiles][4], ao[kTiles][4];
 #pragma unroll
@@ -234,39 +242,60 @@ __global__ void __launch_bounds__(32 * kWarps, kRows == 8 ? 6 : 4) w4a16_mma_ker
   }
   __syncthreads();
   if (tid == 0) (void)mbar_wait(bar, 0, 50000000ull);  // every copy has landed before the CTA exits (bounded)
-  if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
-    for (int i = tid; i < mt * (kRows / 2); i += blockDim.x) {
-      const int m = i / (kRows / 2), p = i % (kRows / 2);
-      if (2 * p + 1 >= nrows) continue;
-      float gs = 0.f, us = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        gs += red[(w * kMaxM + m) * kRows + 2 * p];
-        us += red[(w * kMaxM + m) * kRows + 2 * p + 1];
-      }
-      a.y[int64_t(m0 + m) * a.ldy + (row0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
-    }
-  } else {
-    for (int i = tid; i < mt * kRows; i += blockDim.x) {
-      const int m = i / kRows, n = i % kRows;
-      if (n >= nrows) continue;
+  // With K split, the cluster's CTAs (K slices of the same rows) meet in the first one's shared memory: it reads
+  // every slice's per-warp partials through distributed shared memory, in a fixed order, and writes y.
+  cg::cluster_group cluster = cg::this_cluster();
+  if (a.ks > 1) cluster.sync();
+  if (kr == 0) {
+    auto slice_sum = [&](int m, int n) {
       float sum = 0.f;
+      for (int r = 0; r < a.ks; ++r) {
+        const float* rr = a.ks > 1 ? cluster.map_shared_rank(red, r) : red;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) sum += red[(w * kMaxM + m) * kRows + n];
-      a.y[int64_t(m0 + m) * a.ldy + row0 + n] = __float2bfloat16_rn(sum);
+        for (int w = 0; w < kWarps; ++w) sum += rr[(w * kMaxM + m) * kRows + n];
+      }
+      return sum;
+    };
+    if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
+      for (int i = tid; i < mt * (kRows / 2); i += blockDim.x) {
+        const int m = i / (kRows / 2), p = i % (kRows / 2);
+        if (2 * p + 1 >= nrows) continue;
+        const float gs = slice_sum(m, 2 * p), us = slice_sum(m, 2 * p + 1);
+        a.y[int64_t(m0 + m) * a.ldy + (row0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
+      }
+    } else {
+      for (int i = tid; i < mt * kRows; i += blockDim.x) {
+        const int m = i / kRows, n = i % kRows;
+        if (n >= nrows) continue;
+        a.y[int64_t(m0 + m) * a.ldy + row0 + n] = __float2bfloat16_rn(slice_sum(m, n));
+      }
     }
   }
+  if (a.ks > 1) cluster.sync();  // the other slices' shared memory stays until the first CTA has read it
 }
 
 int mma_rows(int64_t M) { return M <= 8 ? 8 : 16; }
 
-int mma_smem_bytes(int64_t M, int64_t K, int64_t group) {
-  const int64_t T = K / 16, G = K / group, mt = std::min<int64_t>(M, kMaxM), ZW = (G + 7) / 8;
+int mma_smem_bytes(int64_t M, int64_t K, int64_t Kc, int64_t group) {
+  const int64_t T = Kc / 16, G = K / group, mt = std::min<int64_t>(M, kMaxM), ZW = (G + 7) / 8;
   const int64_t kRows = mma_rows(M);
-  const int64_t bytes = kRows * (K / 2 + 16) + ((kRows * G * 2 + 15) / 16) * 16 + kRows * ZW * 4 +
+  const int64_t bytes = kRows * (Kc / 2 + 16) + ((kRows * G * 2 + 15) / 16) * 16 + kRows * ZW * 4 +
                         mt * (32 * ((T + 1) & ~1) + 64) + mt * (((T + 1) & ~1) + 2) * 4 + kWarps * kMaxM * kRows * 4 +
                         32;
   return int(bytes);
+}
+
+// CTAs per row tile along K (a cluster, at most 8): doubled while the grid has fewer CTAs than SMs, or while
+// the x staging does not fit; each slice whole groups of at least 256 inputs.
+int mma_ksplit(int64_t M, int64_t N, int64_t K, int64_t group) {
+  const int rows = mma_rows(M);
+  const int64_t tiles = (N + rows - 1) / rows;
+  auto fits = [&](int k) { return K % (int64_t(k) * group) == 0 && (K / k) % 32 == 0 && K / k >= 256; };
+  int ks = 1;
+  while (ks < 8 && fits(2 * ks) &&
+         (tiles * ks < num_sms() || mma_smem_bytes(M, K, K / ks, group) > kSmemLimit))
+    ks *= 2;
+  return ks;
 }
 
 }  // namespace
@@ -274,8 +303,9 @@ int mma_smem_bytes(int64_t M, int64_t K, int64_t group) {
 // The tensor-core path takes K a multiple of 16 and of the group (group a multiple of 16), 16-byte aligned rows,
 // and shapes whose staging fits two CTAs per SM; M is split into chunks of 16 rows.
 bool w4a16_mma_applies(int64_t M, int64_t N, int64_t K, int64_t group) {
-  (void)N;
-  return K % 32 == 0 && group % 32 == 0 && K / 32 >= kWarps && mma_smem_bytes(M, K, group) <= kSmemLimit;
+  if (K % 32 != 0 || group % 32 != 0 || K / 32 < kWarps) return false;
+  const int ks = mma_ksplit(M, N, K, group);
+  return mma_smem_bytes(M, K, K / ks, group) <= kSmemLimit;
 }
 
 int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
@@ -295,28 +325,34 @@ int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* sc
   a.group = int(group);
   a.G = int(K / group);
   a.ZW = (a.G + 7) / 8;
-  a.T = int(K / 16);
-  a.pitch = int(K / 2 + 16);
+  a.ks = mma_ksplit(M, N, K, group);
+  a.Kc = int(K / a.ks);
+  a.T = a.Kc / 16;
+  a.pitch = a.Kc / 2 + 16;
   a.xpitch = 32 * ((a.T + 1) & ~1) + 64;
   const int rows = mma_rows(M);
   a.sbytes = ((rows * a.G * 2 + 15) / 16) * 16;
   a.zbytes = rows * a.ZW * 4;
   a.spitch = ((a.T + 1) & ~1) + 2;
-  const int smem = mma_smem_bytes(M, K, group);
+  const int smem = mma_smem_bytes(M, K, a.Kc, group);
   auto kernel = rows == 8 ? (fused ? w4a16_mma_kernel<true, 8> : w4a16_mma_kernel<false, 8>)
                           : (fused ? w4a16_mma_kernel<true, 16> : w4a16_mma_kernel<false, 16>);
   int st = set_max_smem(reinterpret_cast<const void*>(kernel), smem);
   if (st) return st;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned((N + rows - 1) / rows), unsigned((M + kMaxM - 1) / kMaxM), 1);
+  cfg.gridDim = dim3(unsigned((N + rows - 1) / rows * a.ks), unsigned((M + kMaxM - 1) / kMaxM), 1);
   cfg.blockDim = dim3(32 * kWarps, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = (flags & BPT_FLAG_PDL) ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(a.ks);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = a.ks > 1 ? attr : attr + 1;  // no cluster attribute when K is not split
+  cfg.numAttrs = (a.ks > 1 ? 1 : 0) + ((flags & BPT_FLAG_PDL) ? 1 : 0);
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
   if (err != cudaSuccess) return set_error(BPT_ERR_CUDA, "w4a16 mma launch: %s", cudaGetErrorString(err));
   return BPT_OK;

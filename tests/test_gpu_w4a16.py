@@ -94,10 +94,26 @@ def test_gemm_gate_up_silu():
     torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
 
 
-def test_m16_long_k_takes_the_cuda_core_kernel():
-    # 16 rows of x at K = 6144 do not fit the tensor-core kernel's staging: the CUDA-core kernel runs them
+def test_m16_long_k_splits_k_over_a_cluster():
+    # 16 rows of x at K = 6144: the tensor-core kernel splits K over a cluster of CTAs (their x staging fits)
     check_linear(16, 256, 6144, 128, seed=11)
     check_linear(9, 264, 6144, 128, seed=12)
+
+
+def test_small_n_splits_k_and_matches():
+    # small N leaves SMs idle: K is split over clusters of 2-8 CTAs whose partials meet in distributed shared
+    # memory (plain and fused)
+    from bpt_b200.kernels.w4a16 import interleave_rows, quantize_w4a16, w4a16_gate_up_silu
+
+    for m, n, k in [(1, 1024, 2048), (1, 256, 6144), (4, 512, 4096), (16, 128, 2048)]:
+        check_linear(m, n, k, 128, seed=m + n)
+    gate, up = dense(128, 2048, 31), dense(128, 2048, 32)
+    x = acts(3, 2048, 33)
+    qg, qu = quantize_w4a16(gate.cuda()), quantize_w4a16(up.cuda())
+    got = w4a16_gate_up_silu(x.cuda(), *[interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)])
+    g = ow4.w4a16_linear(x, *[t.cpu() for t in qg], 128).float()
+    u = ow4.w4a16_linear(x, *[t.cpu() for t in qu], 128).float()
+    torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
 
 
 def test_symmetric_layout_without_zero_points():
