@@ -41,10 +41,6 @@ __host__ __device__ inline PersistLayout persist_layout(int Hkv, int Hq, int q_e
   return p;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Atomic add at GPU scope with release (prior writes, and those ordered before by a barrier, are visible first)
 // and acquire (later reads see what the other arrivals released) semantics; returns the old value.
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(unsigned int* p, uint32_t v) {

@@ -227,19 +227,28 @@ bool w4a16_mma_applies(int64_t M, int64_t N, int64_t K, int64_t group);
 int w4a16_mma(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
               int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
 
+bool w4a16_stream_applies(int64_t M, int64_t N, int64_t K, int64_t group, bool zeros);
+int w4a16_stream(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
+                 void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
+                 cudaStream_t stream);
+
 bool w4a16_gemm_applies(int64_t M, int64_t N, int64_t K, int64_t group);
 int w4a16_gemm(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
                int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
 
-// M >= 32: the tiled tensor-core GEMM (w4a16_gemm.cu). Small M: the tensor-core GEMV (w4a16_mma.cu) where its
-// staging fits, the CUDA-core kernel below otherwise.
+// M >= 32: the tiled tensor-core GEMM (w4a16_gemm.cu). M <= 8: the persistent streaming GEMV (w4a16_stream.cu).
+// Otherwise the tensor-core GEMV (w4a16_mma.cu) where its staging fits, the CUDA-core kernel below last.
 int w4a16_gemv(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                cudaStream_t stream) {
   static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
   if (!cuda_cores && w4a16_gemm_applies(M, N, K, group))
     return w4a16_gemm(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
-  // (it stages the scales and zero points with bulk copies: both 16-byte aligned)
+  // (both stage the scales and zero points with bulk copies: 16-byte aligned)
+  static const bool no_stream = std::getenv("BPT_W4A16_NO_STREAM") != nullptr;
+  if (!cuda_cores && !no_stream && w4a16_stream_applies(M, N, K, group, qzeros != nullptr) && aligned16(scales) &&
+      (!qzeros || aligned16(qzeros)))
+    return w4a16_stream(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
   if (!cuda_cores && w4a16_mma_applies(M, N, K, group) && aligned16(scales) && (!qzeros || aligned16(qzeros)))
     return w4a16_mma(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
   GemvArgs a;

@@ -1,0 +1,323 @@
+// W4A16 linear for M <= 8 tokens as a persistent streaming GEMV: y[M, N] = x[M, K] . (scale * (q - zero))^T.
+//
+// At most one CTA per SM. CTA b owns the contiguous 16-row weight tiles [b T / P, (b + 1) T / P). A producer
+// warp streams each tile (16 code rows, the tile's fp16 scales and zero-point words) into a ring of shared-memory
+// stages with bulk copies (TMA engine), all issued before the kernel waits on its predecessor: the weights do not
+// depend on it. The CTA asks for at most ~113 KB of shared memory and ~32 K registers, so under programmatic
+// dependent launch the next call's CTAs sit beside this one's and fetch their weights while this one computes.
+// Eight consumer warps split K by whole groups; each keeps its groups' x in registers and runs them against every
+// tile of the CTA, so x is read once per CTA and the tiles' code words are the only shared-memory traffic.
+//
+// mma.sync m16n8k16 bf16 -> fp32 with the WEIGHTS as A (the 16 rows of a tile) and the tokens as B (up to 8
+// columns). K is walked in blocks of 64 inputs (4 k-steps u = 0..3). In a block, lane (g, c) owns code words
+// 2c and 2c + 1 (inputs 16c .. 16c + 15 of the block) of rows g and g + 8, read with one 8-byte load per row, and
+// step u takes from them:
+//   A k slots (2c, 2c+1)   = (128 + q, as bf16) of inputs 16c + u, 16c + u + 4      (word 2c >> 4u, LOP3 mask)
+//   A k slots (2c+8, 2c+9) = inputs 16c + 8 + u, 16c + 12 + u                        (word 2c + 1 >> 4u)
+// minus bf16 (128 + z) with one HSUB2: q - z exactly. B holds x at the same inputs (so each lane's B words come
+// from the 32 bytes of x at inputs 16c .. 16c + 15, loaded straight from global memory). Over u and c every input
+// of the block is used once. The MMA sums x (q - z) over a group in fp32; the group's scale multiplies the sum.
+// The warps' partial sums meet in shared memory in a fixed order: results are deterministic.
+#include "common.cuh"
+
+namespace bpt {
+namespace {
+
+constexpr int kRows = 16;                        // weight rows per tile (the MMA's M)
+constexpr int kConsumers = 8;                    // consumer warps (K split), two per SM sub-partition
+constexpr int kThreads = 32 * (kConsumers + 1);  // + the producer warp
+constexpr int kMaxTok = 8;                       // tokens per launch (the MMA's N)
+constexpr int kChunk = 4;                        // tiles a warp holds partial sums for at once
+constexpr int kBudgetShared = 113 * 1024;        // two CTAs per SM (this call's and the next one's)
+constexpr int kBudgetAlone = 220 * 1024;         // when two stages do not fit
+
+struct StreamArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const uint8_t* qweight;  // [N, K/2] bytes
+  const __half* scales;    // [N, G]
+  const uint32_t* qzeros;  // [N, ZW] or null (symmetric: zero point 8)
+  __nv_bfloat16* y;
+  int64_t ldy;
+  int M, N, K, G, ZW;
+  int tiles;   // N / 16
+  int pitch;   // bytes per staged code row: K/2 + 32 (the 8-byte reads of a half warp fall on distinct banks)
+  int sbytes;  // a tile's scales: 16 G fp16 = 32 G bytes
+  int zbytes;  // a tile's zero-point words: 16 ZW u32 (0 without zero points)
+  int stage;   // bytes per ring stage: 16 pitch + sbytes + zbytes
+  int ns;      // ring stages
+};
+
+struct StreamLayout {
+  int ring, red, bars, total;
+};
+
+// ring [ns][stage] | partial sums [2][warps][16 rows][M] f32 | mbarriers full[ns], empty[ns]
+__host__ __device__ inline StreamLayout stream_layout(int M, int stage, int ns) {
+  StreamLayout l;
+  l.ring = 0;
+  l.red = ns * stage;
+  l.bars = l.red + ((2 * kConsumers * kRows * M * 4 + 15) & ~15);
+  l.total = l.bars + 2 * ns * 8;
+  return l;
+}
+
+__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The bf16 pair (q - z) of nibbles u and u + 4 of a code word, given zz = bf16x2 (128 + z): exact.
+__device__ __forceinline__ uint32_t codes_minus_zero(uint32_t w, int u, uint32_t zz) {
+  const uint32_t t = ((w >> (4 * u)) & 0x000F000Fu) | 0x43004300u;  // bf16 (128 + q_u, 128 + q_u+4)
+  __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&t);
+  v = __hsub2(v, *reinterpret_cast<const __nv_bfloat162*>(&zz));
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumers) : "memory"); }
+
+template <bool FUSED, int SPG>  // SPG: k-steps per group (group / 16): 4 or 8
+__global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamArgs a) {
+  constexpr int kBlocks = SPG / 4;  // 64-input blocks per group
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int P = gridDim.x;
+  const int tb = int(int64_t(blockIdx.x) * a.tiles / P), te = int(int64_t(blockIdx.x + 1) * a.tiles / P);
+  const int nt = te - tb;
+  const StreamLayout L = stream_layout(a.M, a.stage, a.ns);
+  uint8_t* ring = smem + L.ring;
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + a.ns;
+
+  if (tid == 0) {
+    for (int s = 0; s < a.ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();  // the next call may now place its CTAs beside this one and fetch its weights
+
+  if (warp == 0) {  // producer: every tile's copies, refilling a stage once the consumers release it
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      const int row_bytes = a.K >> 1;
+      const uint32_t tx = uint32_t(kRows * row_bytes + a.sbytes + a.zbytes);
+      for (int j = 0; j < nt; ++j) {
+        const int s = j % a.ns;
+        if (j >= a.ns && !mbar_wait_sleep(&empty[s], uint32_t((j / a.ns - 1) & 1), 64u)) break;
+        uint8_t* st = ring + s * a.stage;
+        const int64_t row0 = int64_t(tb + j) * kRows;
+        mbar_arrive_expect_tx(&full[s], tx);
+        for (int r = 0; r < kRows; ++r)
+          bulk_g2s_evict_first(st + r * a.pitch, a.qweight + (row0 + r) * row_bytes, uint32_t(row_bytes), &full[s],
+                               policy);
+        bulk_g2s(st + kRows * a.pitch, a.scales + row0 * a.G, uint32_t(a.sbytes), &full[s]);
+        if (a.zbytes) bulk_g2s(st + kRows * a.pitch + a.sbytes, a.qzeros + row0 * a.ZW, uint32_t(a.zbytes), &full[s]);
+      }
+    }
+    return;  // the consumers wait for every copy before the CTA exits
+  }
+
+  const int cw = warp - 1, ctid = tid - 32;
+  const int g = lane >> 2, c = lane & 3;
+  const int gb = cw * a.G / kConsumers, ge = (cw + 1) * a.G / kConsumers;  // this warp's groups
+  constexpr int group = SPG * 16;
+  // B column g is token g (columns past M repeat the last token and are never stored)
+  const __nv_bfloat16* xg = a.x + int64_t(min(g, a.M - 1)) * a.ldx + 16 * c;
+  pdl_wait();  // x (and y) belong to the previous kernel until here
+
+  const int chunk = min(kChunk, a.ns);  // tiles resident together
+  for (int j0 = 0; j0 < nt; j0 += chunk) {
+    const int j1 = min(nt, j0 + chunk);
+    bool ok = true;
+    for (int j = j0; j < j1; ++j) ok = mbar_wait_warp(&full[j % a.ns], uint32_t((j / a.ns) & 1)) && ok;
+    float tot[kChunk][4] = {};  // per tile: D[row g][tok 2c, 2c + 1], D[row g + 8][tok 2c, 2c + 1]
+    if (ok) {
+      for (int grp = gb; grp < ge; ++grp) {
+        // this group's B words: block b, step u -> xb[b][2u] (inputs 16c + u, + u + 4), xb[b][2u + 1] (+8, +12)
+        uint32_t xb[kBlocks][8];
+#pragma unroll
+        for (int b = 0; b < kBlocks; ++b) {
+          const uint4* src = reinterpret_cast<const uint4*>(xg + int64_t(grp) * group + 64 * b);
+          const uint4 lo = src[0], hi = src[1];  // inputs 16c .. 16c + 7, 16c + 8 .. 16c + 15 (bf16 pairs)
+          const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t sel = (u & 1) ? 0x7632u : 0x5410u;  // input i is half (i & 1) of word i >> 1
+            xb[b][2 * u] = __byte_perm(w[u >> 1], w[2 + (u >> 1)], sel);
+            xb[b][2 * u + 1] = __byte_perm(w[4 + (u >> 1)], w[6 + (u >> 1)], sel);
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < kChunk; ++jj) {
+          const int j = j0 + jj;
+          if (j >= j1) break;
+          const uint8_t* st = ring + (j % a.ns) * a.stage;
+          const __half* sc = reinterpret_cast<const __half*>(st + kRows * a.pitch);
+          const uint32_t* zw = reinterpret_cast<const uint32_t*>(st + kRows * a.pitch + a.sbytes);
+          uint32_t z0 = 8u, z1 = 8u;  // symmetric layout: zero point 8
+          if (a.zbytes) {
+            z0 = (zw[g * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u;
+            z1 = (zw[(g + 8) * a.ZW + (grp >> 3)] >> (4 * (grp & 7))) & 15u;
+          }
+          const uint32_t zz0 = (0x4300u | z0) * 0x10001u, zz1 = (0x4300u | z1) * 0x10001u;  // bf16x2 128 + z
+          const float s0 = __half2float(sc[g * a.G + grp]), s1 = __half2float(sc[(g + 8) * a.G + grp]);
+          const uint8_t* ra = st + g * a.pitch + grp * (group / 2) + 8 * c;
+          const uint8_t* rb = ra + 8 * a.pitch;
+          float ae[4] = {0.f, 0.f, 0.f, 0.f}, ao[4] = {0.f, 0.f, 0.f, 0.f};  // even and odd steps: two chains
+#pragma unroll
+          for (int b = 0; b < kBlocks; ++b) {
+            const uint2 wa = *reinterpret_cast<const uint2*>(ra + 32 * b);  // row g: words 2c, 2c + 1 of block b
+            const uint2 wb = *reinterpret_cast<const uint2*>(rb + 32 * b);  // row g + 8
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              mma_bf16((u & 1) ? ao : ae, codes_minus_zero(wa.x, u, zz0), codes_minus_zero(wb.x, u, zz1),
+                       codes_minus_zero(wa.y, u, zz0), codes_minus_zero(wb.y, u, zz1), xb[b][2 * u], xb[b][2 * u + 1]);
+          }
+          tot[jj][0] += s0 * (ae[0] + ao[0]);
+          tot[jj][1] += s0 * (ae[1] + ao[1]);
+          tot[jj][2] += s1 * (ae[2] + ao[2]);
+          tot[jj][3] += s1 * (ae[3] + ao[3]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0)
+      for (int j = j0; j < j1; ++j) mbar_arrive(&empty[j % a.ns]);  // done with these stages (even on a timeout)
+    // per tile: partials in red[j & 1][warp][row][token] (the next tile uses the other half), reduced in a fixed
+    // order over the warps by the threads of (token, row) items
+#pragma unroll
+    for (int jj = 0; jj < kChunk; ++jj) {
+      const int j = j0 + jj;
+      if (j >= j1) break;
+      float* rw = red + ((j & 1) * kConsumers + cw) * kRows * a.M;
+      if (2 * c < a.M) {
+        rw[g * a.M + 2 * c] = tot[jj][0];
+        rw[(g + 8) * a.M + 2 * c] = tot[jj][2];
+      }
+      if (2 * c + 1 < a.M) {
+        rw[g * a.M + 2 * c + 1] = tot[jj][1];
+        rw[(g + 8) * a.M + 2 * c + 1] = tot[jj][3];
+      }
+      consumers_sync();
+      const float* rr = red + (j & 1) * kConsumers * kRows * a.M;
+      const int64_t row0 = int64_t(tb + j) * kRows;
+      if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
+        for (int i = ctid; i < a.M * (kRows / 2); i += 32 * kConsumers) {
+          const int m = i / (kRows / 2), p = i % (kRows / 2);
+          float gs = 0.f, us = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumers; ++w) {
+            gs += rr[(w * kRows + 2 * p) * a.M + m];
+            us += rr[(w * kRows + 2 * p + 1) * a.M + m];
+          }
+          a.y[int64_t(m) * a.ldy + (row0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
+        }
+      } else {
+        for (int i = ctid; i < a.M * kRows; i += 32 * kConsumers) {
+          const int m = i / kRows, r = i % kRows;
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumers; ++w) v += rr[(w * kRows + r) * a.M + m];
+          a.y[int64_t(m) * a.ldy + row0 + r] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+  }
+}
+
+struct StreamPlan {
+  int grid = 0, ns = 0, stage = 0, smem = 0;
+};
+
+StreamPlan stream_plan(int64_t M, int64_t N, int64_t K, int64_t group, bool zeros) {
+  StreamPlan p;
+  if (M < 1 || M > kMaxTok || N % kRows != 0 || K % 64 != 0 || K % group != 0) return p;
+  if (group != 64 && group != 128) return p;
+  const int64_t tiles = N / kRows;
+  if (tiles < 1 || tiles > (1 << 26)) return p;
+  const int G = int(K / group), ZW = (G + 7) / 8;
+  p.grid = int(std::min<int64_t>(tiles, num_sms()));
+  const int per_cta = int((tiles + p.grid - 1) / p.grid);
+  p.stage = kRows * int(K / 2 + 32) + 32 * G + (zeros ? kRows * ZW * 4 : 0);
+  const int fixed = stream_layout(int(M), p.stage, 0).total;
+  const int need = std::min(per_cta, 2);
+  for (int budget : {kBudgetShared, kBudgetAlone}) {
+    const int fit = (budget - fixed) / (p.stage + 16);  // each stage adds its two mbarriers too
+    p.ns = std::min(per_cta, fit);
+    if (p.ns >= need) break;
+  }
+  if (p.ns < need || p.ns < 1) {
+    p.grid = 0;
+    return p;
+  }
+  p.smem = stream_layout(int(M), p.stage, p.ns).total;
+  return p;
+}
+
+}  // namespace
+
+// The streaming GEMV takes M <= 8, N a multiple of 16, K a multiple of 64, groups of 64 or 128, and the scales and
+// zero points 16-byte aligned (checked by the caller).
+bool w4a16_stream_applies(int64_t M, int64_t N, int64_t K, int64_t group, bool zeros) {
+  return stream_plan(M, N, K, group, zeros).grid > 0;
+}
+
+int w4a16_stream(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
+                 void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
+                 cudaStream_t stream) {
+  const StreamPlan plan = stream_plan(M, N, K, group, qzeros != nullptr);
+  if (!plan.grid) return set_error(BPT_ERR_UNSUPPORTED, "w4a16 stream: unsupported shape");
+  StreamArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.qweight = reinterpret_cast<const uint8_t*>(qweight);
+  a.scales = static_cast<const __half*>(scales);
+  a.qzeros = reinterpret_cast<const uint32_t*>(qzeros);
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.M = int(M);
+  a.N = int(N);
+  a.K = int(K);
+  a.G = int(K / group);
+  a.ZW = (a.G + 7) / 8;
+  a.tiles = int(N / kRows);
+  a.pitch = int(K / 2 + 32);
+  a.sbytes = 32 * a.G;
+  a.zbytes = qzeros ? kRows * a.ZW * 4 : 0;
+  a.stage = plan.stage;
+  a.ns = plan.ns;
+  const void* kernel = nullptr;
+  if (group == 64) kernel = fused ? reinterpret_cast<const void*>(w4a16_stream_kernel<true, 4>)
+                                  : reinterpret_cast<const void*>(w4a16_stream_kernel<false, 4>);
+  if (group == 128) kernel = fused ? reinterpret_cast<const void*>(w4a16_stream_kernel<true, 8>)
+                                   : reinterpret_cast<const void*>(w4a16_stream_kernel<false, 8>);
+  if (!kernel) return set_error(BPT_ERR_UNSUPPORTED, "w4a16 stream: group %lld", (long long)group);
+  int st = set_max_smem(kernel, plan.smem);
+  if (st) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(plan.grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & BPT_FLAG_PDL) ? 1 : 0;
+  void* args[] = {&a};
+  cudaError_t err = cudaLaunchKernelExC(&cfg, kernel, args);
+  if (err != cudaSuccess) return set_error(BPT_ERR_CUDA, "w4a16 stream launch: %s", cudaGetErrorString(err));
+  return BPT_OK;
+}
+
+}  // namespace bpt

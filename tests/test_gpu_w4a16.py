@@ -116,6 +116,39 @@ def test_small_n_splits_k_and_matches():
     torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("m,n,k,group", [(1, 16, 256, 64), (2, 4096, 2048, 32), (8, 2048, 6144, 128),
+                                         (7, 512, 6144, 64), (1, 12288, 2048, 128), (3, 160, 4096, 128)])
+def test_streaming_gemv_shapes(m, n, k, group):
+    # M <= 8, N a multiple of 16: the persistent streaming GEMV (one tile to six tiles per CTA, ring refills,
+    # groups of 32/64/128, x staging beside one stage only at K = 6144, M = 8)
+    check_linear(m, n, k, group, seed=m * 7 + n)
+    check_linear(m, n, k, group, seed=m * 7 + n + 1, symmetric=True)
+
+
+def test_streaming_gemv_chain_under_pdl():
+    # each call's weights are fetched before it waits on its predecessor; its x is the predecessor's output
+    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_linear
+
+    k = 2048
+    ws = [quantize_w4a16(dense(k, k, seed=40 + i).cuda()) for i in range(6)]
+    x = acts(2, k, 46).cuda()
+    plain, h = [], x
+    for w in ws:
+        h = w4a16_linear(h, *w)
+        plain.append(h)
+    torch.cuda.synchronize()
+    outs = [torch.empty(2, k, dtype=torch.bfloat16, device="cuda") for _ in ws]
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            h = x
+            for w, o in zip(ws, outs, strict=True):
+                h = w4a16_linear(h, *w, out=o, pdl=True)
+    torch.cuda.synchronize()
+    for want, got in zip(plain, outs, strict=True):
+        assert torch.equal(got, want)
+
+
 def test_symmetric_layout_without_zero_points():
     check_linear(1, 512, 1024, 128, symmetric=True)
 
