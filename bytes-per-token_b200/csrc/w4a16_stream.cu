@@ -27,7 +27,7 @@ constexpr int kRows = 16;                        // weight rows per tile (the MM
 constexpr int kConsumers = 8;                    // consumer warps (K split), two per SM sub-partition
 constexpr int kThreads = 32 * (kConsumers + 1);  // + the producer warp
 constexpr int kMaxTok = 8;                       // tokens per launch (the MMA's N)
-constexpr int kChunk = 4;                        // tiles a warp holds partial sums for at once
+constexpr int kChunk = 3;                        // tiles a warp holds partial sums for at once
 constexpr int kBudgetShared = 113 * 1024;        // two CTAs per SM (this call's and the next one's)
 constexpr int kBudgetAlone = 220 * 1024;         // when two stages do not fit
 
@@ -52,12 +52,12 @@ struct StreamLayout {
   int ring, red, bars, total;
 };
 
-// ring [ns][stage] | partial sums [2][warps][16 rows][M] f32 | mbarriers full[ns], empty[ns]
+// ring [ns][stage] | partial sums [2][chunk tiles][warps][16 rows][M] f32 | mbarriers full[ns], empty[ns]
 __host__ __device__ inline StreamLayout stream_layout(int M, int stage, int ns) {
   StreamLayout l;
   l.ring = 0;
   l.red = ns * stage;
-  l.bars = l.red + ((2 * kConsumers * kRows * M * 4 + 15) & ~15);
+  l.bars = l.red + ((2 * kChunk * kConsumers * kRows * M * 4 + 15) & ~15);
   l.total = l.bars + 2 * ns * 8;
   return l;
 }
@@ -133,22 +133,47 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
   constexpr int group = SPG * 16;
   // B column g is token g (columns past M repeat the last token and are never stored)
   const __nv_bfloat16* xg = a.x + int64_t(min(g, a.M - 1)) * a.ldx + 16 * c;
+  const int chunk = min(kChunk, a.ns);  // tiles resident together
+  // The chunk's stages: tile j sits in stage j mod ns, filled for the (j / ns)-th time; every lane waits itself.
+  // The first chunk's wait comes before the wait on the previous kernel (the weights do not depend on it).
+  auto wait_chunk = [&](int j0, uint32_t* soff) {
+    bool ok = true;
+#pragma unroll
+    for (int jj = 0; jj < kChunk; ++jj) {
+      const int j = j0 + jj;
+      const int s = j % a.ns;
+      soff[jj] = uint32_t(s * a.stage);
+      if (j < min(nt, j0 + chunk)) ok = mbar_wait(&full[s], uint32_t((j / a.ns) & 1)) && ok;
+    }
+    return __all_sync(0xffffffffu, ok);
+  };
+  uint32_t soff[kChunk];
+  bool ok = wait_chunk(0, soff);
   pdl_wait();  // x (and y) belong to the previous kernel until here
 
-  const int chunk = min(kChunk, a.ns);  // tiles resident together
   for (int j0 = 0; j0 < nt; j0 += chunk) {
     const int j1 = min(nt, j0 + chunk);
-    bool ok = true;
-    for (int j = j0; j < j1; ++j) ok = mbar_wait_warp(&full[j % a.ns], uint32_t((j / a.ns) & 1)) && ok;
+    if (j0 > 0) ok = wait_chunk(j0, soff);
     float tot[kChunk][4] = {};  // per tile: D[row g][tok 2c, 2c + 1], D[row g + 8][tok 2c, 2c + 1]
     if (ok) {
+      // x of the group: lane c's inputs 16c .. 16c + 7 and 16c + 8 .. 16c + 15 of each block (bf16 pairs); the
+      // next group's are requested before this group's MMAs
+      uint4 xr[kBlocks][2];
+      auto load_x = [&](int grp) {
+#pragma unroll
+        for (int b = 0; b < kBlocks; ++b) {
+          const uint4* src = reinterpret_cast<const uint4*>(xg + int64_t(grp) * group + 64 * b);
+          xr[b][0] = src[0];
+          xr[b][1] = src[1];
+        }
+      };
+      if (gb < ge) load_x(gb);
       for (int grp = gb; grp < ge; ++grp) {
         // this group's B words: block b, step u -> xb[b][2u] (inputs 16c + u, + u + 4), xb[b][2u + 1] (+8, +12)
         uint32_t xb[kBlocks][8];
 #pragma unroll
         for (int b = 0; b < kBlocks; ++b) {
-          const uint4* src = reinterpret_cast<const uint4*>(xg + int64_t(grp) * group + 64 * b);
-          const uint4 lo = src[0], hi = src[1];  // inputs 16c .. 16c + 7, 16c + 8 .. 16c + 15 (bf16 pairs)
+          const uint4 lo = xr[b][0], hi = xr[b][1];
           const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -157,11 +182,12 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
             xb[b][2 * u + 1] = __byte_perm(w[4 + (u >> 1)], w[6 + (u >> 1)], sel);
           }
         }
+        if (grp + 1 < ge) load_x(grp + 1);
 #pragma unroll
         for (int jj = 0; jj < kChunk; ++jj) {
           const int j = j0 + jj;
           if (j >= j1) break;
-          const uint8_t* st = ring + (j % a.ns) * a.stage;
+          const uint8_t* st = ring + soff[jj];
           const __half* sc = reinterpret_cast<const __half*>(st + kRows * a.pitch);
           const uint32_t* zw = reinterpret_cast<const uint32_t*>(st + kRows * a.pitch + a.sbytes);
           uint32_t z0 = 8u, z1 = 8u;  // symmetric layout: zero point 8
@@ -192,14 +218,16 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
     }
     __syncwarp();
     if (lane == 0)
-      for (int j = j0; j < j1; ++j) mbar_arrive(&empty[j % a.ns]);  // done with these stages (even on a timeout)
-    // per tile: partials in red[j & 1][warp][row][token] (the next tile uses the other half), reduced in a fixed
-    // order over the warps by the threads of (token, row) items
+#pragma unroll
+      for (int jj = 0; jj < kChunk; ++jj)  // done with these stages (even on a timeout)
+        if (j0 + jj < j1) mbar_arrive(&empty[(j0 + jj) % a.ns]);
+    // the chunk's partials in red[chunk parity][tile][warp][row][token] (the next chunk uses the other half), one
+    // barrier, then each (tile, token, row) item is summed over the warps in a fixed order
+    float* rc = red + ((j0 / chunk) & 1) * (kChunk * kConsumers * kRows * a.M);
 #pragma unroll
     for (int jj = 0; jj < kChunk; ++jj) {
-      const int j = j0 + jj;
-      if (j >= j1) break;
-      float* rw = red + ((j & 1) * kConsumers + cw) * kRows * a.M;
+      if (j0 + jj >= j1) break;
+      float* rw = rc + (jj * kConsumers + cw) * kRows * a.M;
       if (2 * c < a.M) {
         rw[g * a.M + 2 * c] = tot[jj][0];
         rw[(g + 8) * a.M + 2 * c] = tot[jj][2];
@@ -208,28 +236,32 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
         rw[g * a.M + 2 * c + 1] = tot[jj][1];
         rw[(g + 8) * a.M + 2 * c + 1] = tot[jj][3];
       }
-      consumers_sync();
-      const float* rr = red + (j & 1) * kConsumers * kRows * a.M;
-      const int64_t row0 = int64_t(tb + j) * kRows;
-      if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
-        for (int i = ctid; i < a.M * (kRows / 2); i += 32 * kConsumers) {
-          const int m = i / (kRows / 2), p = i % (kRows / 2);
-          float gs = 0.f, us = 0.f;
+    }
+    consumers_sync();
+    if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
+      for (int i = ctid; i < (j1 - j0) * a.M * (kRows / 2); i += 32 * kConsumers) {
+        const int jj = i / (a.M * (kRows / 2)), rest = i - jj * (a.M * (kRows / 2));
+        const int m = rest / (kRows / 2), p = rest % (kRows / 2);
+        const float* rr = rc + jj * kConsumers * kRows * a.M;
+        float gs = 0.f, us = 0.f;
 #pragma unroll
-          for (int w = 0; w < kConsumers; ++w) {
-            gs += rr[(w * kRows + 2 * p) * a.M + m];
-            us += rr[(w * kRows + 2 * p + 1) * a.M + m];
-          }
-          a.y[int64_t(m) * a.ldy + (row0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
+        for (int w = 0; w < kConsumers; ++w) {
+          gs += rr[(w * kRows + 2 * p) * a.M + m];
+          us += rr[(w * kRows + 2 * p + 1) * a.M + m];
         }
-      } else {
-        for (int i = ctid; i < a.M * kRows; i += 32 * kConsumers) {
-          const int m = i / kRows, r = i % kRows;
-          float v = 0.f;
+        const int64_t row0 = int64_t(tb + j0 + jj) * kRows;
+        a.y[int64_t(m) * a.ldy + (row0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
+      }
+    } else {
+      for (int i = ctid; i < (j1 - j0) * a.M * kRows; i += 32 * kConsumers) {
+        const int jj = i / (a.M * kRows), rest = i - jj * (a.M * kRows);
+        const int m = rest / kRows, r = rest % kRows;
+        const float* rr = rc + jj * kConsumers * kRows * a.M;
+        float v = 0.f;
 #pragma unroll
-          for (int w = 0; w < kConsumers; ++w) v += rr[(w * kRows + r) * a.M + m];
-          a.y[int64_t(m) * a.ldy + row0 + r] = __float2bfloat16_rn(v);
-        }
+        for (int w = 0; w < kConsumers; ++w) v += rr[(w * kRows + r) * a.M + m];
+        const int64_t row0 = int64_t(tb + j0 + jj) * kRows;
+        a.y[int64_t(m) * a.ldy + row0 + r] = __float2bfloat16_rn(v);
       }
     }
   }
