@@ -96,6 +96,16 @@ def w4a16_gate_up_silu(x, qweight, scales, qzeros=None, *, group: int = 128, out
     return _linear("bpt_w4a16_gate_up_silu", x, qweight, scales, qzeros, group, out, pdl, qweight.shape[0] // 2)
 
 
+KERNELS = {0: "cuda_cores", 1: "mma_gemv", 2: "stream", 3: "mma_gemm", 4: "tcgen05"}
+
+
+def w4a16_kernel(m: int, n: int, k: int, group: int = 128, zeros: bool = True) -> str:
+    """The kernel `w4a16_linear` launches for this shape (16-byte aligned scales and zero points). "tcgen05"
+    multiplies with the dense bf16 weight round_bf16(s (q - z)) (the reference's dequantize_linear); the others
+    scale each group's fp32 sum of x (q - z)."""
+    return KERNELS[int(lib().bpt_w4a16_kernel(m, n, k, group, 1 if zeros else 0))]
+
+
 def interleave_rows(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """[I, ...] and [I, ...] -> [2I, ...] with row 2i = gate row i and row 2i+1 = up row i."""
     if gate.shape != up.shape:

@@ -4,6 +4,7 @@
     python -m bpt_b200.profile_case attention-config3
     python -m bpt_b200.profile_case gemv-config1
     python -m bpt_b200.profile_case w4a16-sweep
+    python -m bpt_b200.profile_case gate-up-m64      (gate-up-m256)
 
 Each kernel case builds its seeded synthetic inputs once, then launches the kernel `--launches` times back to
 back and prints the mean device time per launch (CUDA events; not a benchmark number under a profiler).
@@ -93,6 +94,17 @@ def _sweep() -> None:
         torch.cuda.empty_cache()
 
 
+def _gate_up(m: int, launches: int) -> float:
+    """The fused gate_up linear of config 4 (12288 x 2048) at M tokens: one weight copy."""
+    from .kernels.w4a16 import w4a16_gate_up_silu
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qw, sc, qz = quantize_w4a16(torch.randn(12288, 2048, generator=g, device="cuda") * 0.02, 128)
+    x = torch.randn(m, 2048, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(m, 6144, dtype=torch.bfloat16, device="cuda")
+    return _time(lambda: w4a16_gate_up_silu(x, qw, sc, qz, out=y), launches)
+
+
 def _peak_gbs() -> float:
     import json
     from pathlib import Path
@@ -115,7 +127,8 @@ def _time(fn, launches: int) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("case", choices=["attention-config2", "attention-config3", "gemv-config1", "w4a16-sweep"])
+    ap.add_argument("case", choices=["attention-config2", "attention-config3", "gemv-config1", "w4a16-sweep",
+                                     "gate-up-m64", "gate-up-m256"])
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
     if args.case == "w4a16-sweep":
@@ -123,6 +136,8 @@ def main() -> None:
         return
     if args.case == "gemv-config1":
         us = _gemv(args.launches)
+    elif args.case.startswith("gate-up-m"):
+        us = _gate_up(int(args.case.split("-m")[1]), args.launches)
     else:
         us = _attention(2 if args.case.endswith("2") else 3, args.launches)
     print(f"{args.case}: {us:.1f} us per launch (mean of {args.launches}, after one warm-up launch)")

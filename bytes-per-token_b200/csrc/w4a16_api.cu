@@ -5,6 +5,7 @@ namespace bpt {
 
 int w4a16_check(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* y,
                 int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused);
+int w4a16_pick(int64_t M, int64_t N, int64_t K, int64_t group, bool zeros, bool aligned);
 int w4a16_gemv(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                cudaStream_t stream);
@@ -82,6 +83,10 @@ extern "C" int bpt_w4a16_gate_up_silu(const void* x, int64_t ldx, const int32_t*
   if (st) return st;
   return w4a16_gemv(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, true, flags,
                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bpt_w4a16_kernel(int64_t M, int64_t N, int64_t K, int64_t group, int has_zeros) {
+  return w4a16_pick(M, N, K, group, has_zeros != 0, true);
 }
 
 extern "C" int bpt_w4a16_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int64_t group, int32_t* qweight,

@@ -232,25 +232,46 @@ int w4a16_stream(const void* x, int64_t ldx, const int32_t* qweight, const void*
                  void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                  cudaStream_t stream);
 
+bool w4a16_tc_applies(int64_t M, int64_t N, int64_t K, int64_t group);
+int w4a16_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
+             int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
+
 bool w4a16_gemm_applies(int64_t M, int64_t N, int64_t K, int64_t group);
 int w4a16_gemm(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
                int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
 
-// M >= 32: the tiled tensor-core GEMM (w4a16_gemm.cu). M <= 8: the persistent streaming GEMV (w4a16_stream.cu).
-// Otherwise the tensor-core GEMV (w4a16_mma.cu) where its staging fits, the CUDA-core kernel below last.
+// The kernel for a shape: M >= 32 the tcgen05 GEMM (w4a16_tc.cu), else the mma.sync tiled GEMM (w4a16_gemm.cu);
+// M <= 8 the persistent streaming GEMV (w4a16_stream.cu); otherwise the tensor-core GEMV (w4a16_mma.cu) where
+// its staging fits, the CUDA-core kernel below last. The bulk-copy kernels need 16-byte aligned scales and zero
+// points. (BPT_W4A16_NO_TC, BPT_W4A16_NO_STREAM and BPT_W4A16_CUDA_CORES in the environment leave kernels out,
+// for comparisons.)
+int w4a16_pick(int64_t M, int64_t N, int64_t K, int64_t group, bool zeros, bool aligned) {
+  static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
+  static const bool no_tc = std::getenv("BPT_W4A16_NO_TC") != nullptr;
+  static const bool no_stream = std::getenv("BPT_W4A16_NO_STREAM") != nullptr;
+  if (cuda_cores) return BPT_W4A16_KERNEL_CUDA_CORES;
+  if (!no_tc && w4a16_tc_applies(M, N, K, group)) return BPT_W4A16_KERNEL_TCGEN05;
+  if (w4a16_gemm_applies(M, N, K, group)) return BPT_W4A16_KERNEL_MMA_GEMM;
+  if (aligned && !no_stream && w4a16_stream_applies(M, N, K, group, zeros)) return BPT_W4A16_KERNEL_STREAM;
+  if (aligned && w4a16_mma_applies(M, N, K, group)) return BPT_W4A16_KERNEL_MMA_GEMV;
+  return BPT_W4A16_KERNEL_CUDA_CORES;
+}
+
 int w4a16_gemv(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros,
                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags,
                cudaStream_t stream) {
-  static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
-  if (!cuda_cores && w4a16_gemm_applies(M, N, K, group))
-    return w4a16_gemm(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
-  // (both stage the scales and zero points with bulk copies: 16-byte aligned)
-  static const bool no_stream = std::getenv("BPT_W4A16_NO_STREAM") != nullptr;
-  if (!cuda_cores && !no_stream && w4a16_stream_applies(M, N, K, group, qzeros != nullptr) && aligned16(scales) &&
-      (!qzeros || aligned16(qzeros)))
-    return w4a16_stream(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
-  if (!cuda_cores && w4a16_mma_applies(M, N, K, group) && aligned16(scales) && (!qzeros || aligned16(qzeros)))
-    return w4a16_mma(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
+  switch (w4a16_pick(M, N, K, group, qzeros != nullptr, aligned16(scales) && (!qzeros || aligned16(qzeros)))) {
+    case BPT_W4A16_KERNEL_TCGEN05:
+      return w4a16_tc(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
+    case BPT_W4A16_KERNEL_MMA_GEMM:
+      return w4a16_gemm(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
+    case BPT_W4A16_KERNEL_STREAM:
+      return w4a16_stream(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
+    case BPT_W4A16_KERNEL_MMA_GEMV:
+      return w4a16_mma(x, ldx, qweight, scales, qzeros, y, ldy, M, N, K, group, fused, flags, stream);
+    default:
+      break;
+  }
   GemvArgs a;
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.ldx = ldx;

@@ -77,6 +77,20 @@ int bpt_w4a16_gate_up_silu(const void* x, int64_t ldx, const int32_t* qweight, c
                            const int32_t* qzeros, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                            int64_t group, int flags, void* stream);
 
+/* Which kernel bpt_w4a16_linear / bpt_w4a16_gate_up_silu launch for a shape (given 16-byte aligned scales and zero
+ * points), and so which arithmetic produces y:
+ *   BPT_W4A16_KERNEL_TCGEN05    M >= 32: the dense bf16 weight round_bf16(scale * (q - zero)) (one rounding, as
+ *                               quant/compressed.py:56-69 builds it) contracted on the tcgen05 tensor cores, fp32
+ *                               accumulation;
+ *   the others                  every group's sum of x (q - zero) in fp32, times the fp32 scale (no weight rounding).
+ * Returns a BPT_W4A16_KERNEL_* value. */
+#define BPT_W4A16_KERNEL_CUDA_CORES 0
+#define BPT_W4A16_KERNEL_MMA_GEMV 1
+#define BPT_W4A16_KERNEL_STREAM 2
+#define BPT_W4A16_KERNEL_MMA_GEMM 3
+#define BPT_W4A16_KERNEL_TCGEN05 4
+int bpt_w4a16_kernel(int64_t M, int64_t N, int64_t K, int64_t group, int has_zeros);
+
 /* RTN-quantize a dense weight W [N, K] (bf16 or fp32, row-major) to the W4A16 format above: per group of
  * `group` inputs, scale = fp16((max(w,0) - min(w,0)) / 15) (1.0 for an all-zero group), zero =
  * round(-min / scale), code = clamp(round(w / scale) + zero, 0, 15), rounding half to even.

@@ -120,16 +120,21 @@ def w4a16_linear(
     qzeros: torch.Tensor | None,
     group: int = 128,
     bias: torch.Tensor | None = None,
+    dense_bf16: bool = False,
 ) -> torch.Tensor:
     """y = x @ W^T in fp32 from the packed format, returned in x's dtype.
 
     The reference path: unpack (compressed.py:44-53), dequantize (rtn.py:103-104), then a float32
     `F.linear` (engine/model.py:43-46 runs nn.Linear), rounded once to the activation dtype.
+    dense_bf16: the weight the reference's model actually holds, `dequantize_linear` (compressed.py:56-69):
+    each product s (q - z), exact in float32, rounded once to bf16, then the fp32-accumulated matmul.
     """
     n, k = qweight.shape[0], qweight.shape[1] * 8
     codes = unpack_nibbles_int32(qweight, k)
     zeros = None if qzeros is None else unpack_nibbles_int32(qzeros, k // group)
     w = dequantize_w4a16(codes, scales, zeros, group)
+    if dense_bf16:
+        w = w.to(torch.bfloat16).float()
     y = torch.nn.functional.linear(x.float(), w, None if bias is None else bias.float())
     return y.to(x.dtype)
 

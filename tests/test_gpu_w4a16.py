@@ -37,21 +37,28 @@ def test_quantize_is_bit_exact(n, k, group):
 
 
 def check_linear(m, n, k, group, seed=0, symmetric=False):
-    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_linear
+    """The kernel against the oracle of its arithmetic: the tcgen05 GEMM multiplies with the reference model's
+    dense bf16 weight (compressed.py:56-69), the others scale exact group sums in fp32."""
+    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_kernel, w4a16_linear
 
     w = dense(n, k, seed)
     x = acts(m, k, seed + 1)
     qweight, scales, qzeros = quantize_w4a16(w.cuda(), group)
     if symmetric:
         qzeros = None
+    dense_bf16 = w4a16_kernel(m, n, k, group, zeros=qzeros is not None) == "tcgen05"
     got = w4a16_linear(x.cuda(), qweight, scales, qzeros, group=group)
-    want = ow4.w4a16_linear(x, qweight.cpu(), scales.cpu(), None if qzeros is None else qzeros.cpu(), group)
+    want = ow4.w4a16_linear(x, qweight.cpu(), scales.cpu(), None if qzeros is None else qzeros.cpu(), group,
+                            dense_bf16=dense_bf16)
     assert got.dtype == torch.bfloat16 and got.shape == (m, n)
     torch.testing.assert_close(got.cpu().float(), want.float(), **TOL)
     # and much tighter than the tolerance against an fp64 evaluation of the same quantized weight
     codes = ow4.unpack_nibbles_int32(qweight.cpu(), k)
     zeros = None if qzeros is None else ow4.unpack_nibbles_int32(qzeros.cpu(), k // group)
-    exact = x.double() @ ow4.dequantize_w4a16(codes, scales.cpu(), zeros, group).double().T
+    wq = ow4.dequantize_w4a16(codes, scales.cpu(), zeros, group)
+    if dense_bf16:
+        wq = wq.to(torch.bfloat16).float()
+    exact = x.double() @ wq.double().T
     err = (got.cpu().double() - exact).abs().max().item()
     assert err <= 2 ** -8 * exact.abs().max().item() + 1e-6
 
