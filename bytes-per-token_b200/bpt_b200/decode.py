@@ -10,8 +10,10 @@ then the final norm, the tied LM head and a greedy pick. The hot-path pieces run
 - the FP8 KV write (`quantize_kv_paged`) at slot `length % 16` of block `block_table[b, length // 16]`;
 - paged FP8 decode attention (`attend`, the persistent fused-merge kernel).
 
-RMSNorm (`engine/model.py:24-36`), RoPE (`engine/rope.py:18-43`), the embedding and the LM head stay in PyTorch,
-as the reference computes them. Weights are random (no checkpoints here): N(0, 0.02), quantized to INT4 g128
+With `fused=True` (the default) the small ops around them are two fused kernels per use (`decode_fused.py`):
+the residual adds with the following RMSNorm (`engine/model.py:24-36, 109-111`), and q_norm / k_norm, RoPE and
+the FP8 cache write of the new token in one pass; `fused=False` runs them as the reference's PyTorch ops (plus
+`quantize_kv_paged`). The embedding and the LM head stay in PyTorch. Weights are random (no checkpoints here): N(0, 0.02), quantized to INT4 g128
 by `quantize_w4a16`; the LM head stays bf16 and tied to the embedding (`quant/model.py:3-4`). The KV pools hold
 random finite E4M3 codes for the existing context. All buffers are allocated up front, so `step` can be
 captured in a CUDA graph (`capture`).
@@ -24,6 +26,7 @@ from dataclasses import dataclass, field
 
 import torch
 
+from bpt_b200.kernels.decode_fused import qk_norm_rope_kv_write, rms_norm_residual
 from bpt_b200.kernels.kv_attention import PagedQuantKV, attend, attend_workspace, paged_split
 from bpt_b200.kernels.kv_write import quantize_kv_paged
 from bpt_b200.kernels.w4a16 import interleave_rows, quantize_w4a16, w4a16_gate_up_silu, w4a16_linear
@@ -96,8 +99,8 @@ class Qwen3Decoder:
     """
 
     def __init__(self, dims: Qwen3Dims, lengths: torch.Tensor, *, device="cuda", seed: int = 0, capacity: int = 64,
-                 kv_scale: float = 1.0 / 64, keep_dense: bool = False):
-        self.dims, self.device = dims, torch.device(device)
+                 kv_scale: float = 1.0 / 64, keep_dense: bool = False, fused: bool = True):
+        self.dims, self.device, self.fused = dims, torch.device(device), fused
         d, dev = dims, self.device
         g = torch.Generator(device=dev).manual_seed(seed)
         lengths = lengths.to(torch.int64).cpu()
@@ -148,6 +151,10 @@ class Qwen3Decoder:
         self.attn = torch.empty(b, d.q_heads, d.head_dim, dtype=torch.bfloat16, device=dev)
         self.proj = torch.empty(b, d.hidden, dtype=torch.bfloat16, device=dev)
         self.act = torch.empty(b, d.intermediate, dtype=torch.bfloat16, device=dev)
+        self.h = torch.empty(b, d.hidden, dtype=torch.bfloat16, device=dev)  # residual stream (fused path)
+        self.h2 = torch.empty(b, d.hidden, dtype=torch.bfloat16, device=dev)
+        self.x = torch.empty(b, d.hidden, dtype=torch.bfloat16, device=dev)  # normed input of the next linear
+        self.q = torch.empty(b, d.q_heads, d.head_dim, dtype=torch.bfloat16, device=dev)
         split = paged_split(b, self.max_tokens, 16, torch.cuda.get_device_properties(dev).multi_processor_count)
         self.split = split
         self.workspace = attend_workspace(b, d.q_heads, d.head_dim, -(-self.max_tokens // split), dev).clone()
@@ -176,18 +183,44 @@ class Qwen3Decoder:
         w4a16_linear(self.act, *layer.down, group=d.group, out=self.proj, pdl=True)
         return h + self.proj
 
+    def layers_fused(self, cos, sin, write_blocks, write_offsets, lengths_after) -> torch.Tensor:
+        """Every layer on the fused kernels; self.h holds the embedded tokens. Returns the final-normed hidden.
+
+        Each residual add is fused with the RMSNorm that follows it: the attention residual with the
+        post-attention norm, the MLP residual with the next layer's input norm (the final norm after the last)."""
+        d, b = self.dims, self.batch
+        qd = d.q_heads * d.head_dim
+        rms_norm_residual(self.h, self.layers[0].input_norm, d.eps, x_out=self.x, pdl=True)
+        for i, layer in enumerate(self.layers):
+            w4a16_linear(self.x, *layer.qkv, group=d.group, out=self.qkv, pdl=True)
+            qk_norm_rope_kv_write(self.qkv, d.q_heads, d.kv_heads, layer.q_norm, layer.k_norm, cos, sin, d.eps,
+                                  layer.kv, write_blocks, write_offsets, q_out=self.q, pdl=True)
+            attend(self.q, layer.kv, lengths_after, self.scale, out=self.attn, workspace=self.workspace,
+                   tokens=self.max_tokens, split=self.split, pdl=True)
+            w4a16_linear(self.attn.view(b, qd), *layer.o, group=d.group, out=self.proj, pdl=True)
+            rms_norm_residual(self.h, layer.post_norm, d.eps, delta=self.proj, h_out=self.h2, x_out=self.x, pdl=True)
+            w4a16_gate_up_silu(self.x, *layer.gate_up, group=d.group, out=self.act, pdl=True)
+            w4a16_linear(self.act, *layer.down, group=d.group, out=self.proj, pdl=True)
+            nxt = self.layers[i + 1].input_norm if i + 1 < len(self.layers) else self.final_norm
+            rms_norm_residual(self.h2, nxt, d.eps, delta=self.proj, h_out=self.h, x_out=self.x, pdl=True)
+        return self.x
+
     def step_body(self) -> torch.Tensor:
         """Embed self.tokens, run every layer, pick the next tokens (greedy), advance the lengths."""
         d = self.dims
-        h = self.embed[self.tokens]
         pos = self.lengths.to(torch.int64)
         cos, sin = rope_cos_sin(pos, d.head_dim, d.rope_theta, torch.bfloat16)
         write_blocks = torch.gather(self.block_table, 1, (pos // self.block_size)[:, None]).to(torch.int32)
         write_offsets = (pos % self.block_size).to(torch.int32)[:, None]
         lengths_after = self.lengths + 1
-        for layer in self.layers:
-            h = self.layer_forward(layer, h, cos, sin, write_blocks, write_offsets, lengths_after)
-        h = rms_norm(h, self.final_norm, d.eps)
+        if self.fused:
+            torch.index_select(self.embed, 0, self.tokens, out=self.h)
+            h = self.layers_fused(cos, sin, write_blocks, write_offsets, lengths_after)
+        else:
+            h = self.embed[self.tokens]
+            for layer in self.layers:
+                h = self.layer_forward(layer, h, cos, sin, write_blocks, write_offsets, lengths_after)
+            h = rms_norm(h, self.final_norm, d.eps)
         logits = h @ self.embed.T
         nxt = logits.argmax(dim=-1)
         self.lengths.add_(1)

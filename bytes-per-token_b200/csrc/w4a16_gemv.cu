@@ -240,7 +240,7 @@ bool w4a16_gemm_applies(int64_t M, int64_t N, int64_t K, int64_t group);
 int w4a16_gemm(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const int32_t* qzeros, void* y,
                int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group, bool fused, int flags, cudaStream_t stream);
 
-// The kernel for a shape: M >= 32 the tcgen05 GEMM (w4a16_tc.cu), else the mma.sync tiled GEMM (w4a16_gemm.cu);
+// The kernel for a shape: M >= 16 the tcgen05 GEMM (w4a16_tc.cu), else the mma.sync tiled GEMM (w4a16_gemm.cu);
 // M <= 8 the persistent streaming GEMV (w4a16_stream.cu); otherwise the tensor-core GEMV (w4a16_mma.cu) where
 // its staging fits, the CUDA-core kernel below last. The bulk-copy kernels need 16-byte aligned scales and zero
 // points. (BPT_W4A16_NO_TC, BPT_W4A16_NO_STREAM and BPT_W4A16_CUDA_CORES in the environment leave kernels out,

@@ -1,9 +1,9 @@
-// W4A16 linear for M >= 32 tokens on the 5th-generation tensor cores (tcgen05, sm_100a only):
+// W4A16 linear for M >= 16 tokens on the 5th-generation tensor cores (tcgen05, sm_100a only):
 //   y[M, N] = x[M, K] . W^T,   W[n][k] = bf16(scale[n][g] * (q[n][k] - zero[n][g])),   fp32 accumulation,
 // i.e. the dense bf16 weight that the reference's dequantize-then-nn.Linear path multiplies with (one rounding per
 // weight), contracted on the tensor cores.
 //
-// CTA tile: 128 weight rows (the UMMA M) x BN tokens (the UMMA N: 32, 64 or 128) x a slice of K; K is split over a
+// CTA tile: 128 weight rows (the UMMA M) x BN tokens (the UMMA N: 16, 32, 64 or 128) x a slice of K; K is split over a
 // thread-block cluster of `ks` CTAs (partial tiles reduced through distributed shared memory) when the row tiles
 // alone leave SMs idle. K advances in chunks of 64 inputs (one 128-byte swizzle atom of bf16):
 //   two producer warps (one lane each): TMA loads of the chunk's code tile [128 rows][32 B], and of its x
@@ -458,12 +458,12 @@ struct TcPlan {
 
 TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int64_t group) {
   TcPlan p;
-  if (M < 32 || N < 1 || K % kChunkK != 0 || K < 2 * kChunkK || (group != 64 && group != 128) || K % group != 0)
+  if (M < 16 || N < 1 || K % kChunkK != 0 || K < 2 * kChunkK || (group != 64 && group != 128) || K % group != 0)
     return p;
   if (M >= (1ll << 31) || N >= (1ll << 31)) return p;
-  // tokens per tile: M rounded up to 32 / 64 / 128; more tokens take more tiles (each CTA pair per SM then gets
-  // its own tiles, which beats one 256-token tile per SM)
-  p.bn = M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  // tokens per tile: M rounded up to 16 / 32 / 64 / 128; more tokens take more tiles (each CTA pair per SM then
+  // gets its own tiles, which beats one 256-token tile per SM)
+  p.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   p.token_tiles = int((M + p.bn - 1) / p.bn);
   p.row_tiles = int((N + kTileRows - 1) / kTileRows);
   p.na = 3;  // A stages in tensor memory
@@ -493,7 +493,7 @@ TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int64_t group) {
 
 }  // namespace
 
-// The tcgen05 path takes M >= 32, K a multiple of 64 (at least 128), groups of 64 or 128; x and qweight 16-byte
+// The tcgen05 path takes M >= 16, K a multiple of 64 (at least 128), groups of 64 or 128; x and qweight 16-byte
 // aligned with ldx a multiple of 8 (checked by the caller), and a driver that provides the tensor-map encoder.
 bool w4a16_tc_applies(int64_t M, int64_t N, int64_t K, int64_t group) {
   return tc_plan(M, N, K, group).bn > 0 && encode_fn() != nullptr;
@@ -546,8 +546,8 @@ int w4a16_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
   const void* kernel = nullptr;
 #define BPT_TC_PICK(F, B) \
   if (fused == F && plan.bn == B) kernel = reinterpret_cast<const void*>(w4a16_tc_kernel<F, B>);
-  BPT_TC_PICK(false, 32) BPT_TC_PICK(false, 64) BPT_TC_PICK(false, 128)
-  BPT_TC_PICK(true, 32) BPT_TC_PICK(true, 64) BPT_TC_PICK(true, 128)
+  BPT_TC_PICK(false, 16) BPT_TC_PICK(false, 32) BPT_TC_PICK(false, 64) BPT_TC_PICK(false, 128)
+  BPT_TC_PICK(true, 16) BPT_TC_PICK(true, 32) BPT_TC_PICK(true, 64) BPT_TC_PICK(true, 128)
 #undef BPT_TC_PICK
   if (!kernel) return set_error(BPT_ERR_UNSUPPORTED, "w4a16 tc: no kernel for %d tokens", plan.bn);
   int st = set_max_smem(kernel, plan.smem);

@@ -79,7 +79,7 @@ int bpt_w4a16_gate_up_silu(const void* x, int64_t ldx, const int32_t* qweight, c
 
 /* Which kernel bpt_w4a16_linear / bpt_w4a16_gate_up_silu launch for a shape (given 16-byte aligned scales and zero
  * points), and so which arithmetic produces y:
- *   BPT_W4A16_KERNEL_TCGEN05    M >= 32: the dense bf16 weight round_bf16(scale * (q - zero)) (one rounding, as
+ *   BPT_W4A16_KERNEL_TCGEN05    M >= 16: the dense bf16 weight round_bf16(scale * (q - zero)) (one rounding, as
  *                               quant/compressed.py:56-69 builds it) contracted on the tcgen05 tensor cores, fp32
  *                               accumulation;
  *   the others                  every group's sum of x (q - zero) in fp32, times the fp32 scale (no weight rounding).
@@ -203,6 +203,26 @@ int bpt_paged_kv_write(const void* k, const void* v, int in_dtype, int64_t strid
 int bpt_kivi_quantize(const void* k, const void* v, int in_dtype, int64_t B, int64_t Hkv, int64_t T, int64_t D,
                       int bits, int64_t group, void* k_codes, void* v_codes, void* k_scale, void* k_zero,
                       void* v_scale, void* v_zero, int64_t t_max, int64_t n_groups, int64_t t0, void* stream);
+
+/* ---- the decode step's ops around the hot path (the caller side: config 5's Qwen3 step) -------------------------
+ * bf16 tensors, row-major. RMSNorm of engine/model.py:24-36 with the residual add of DecoderLayer.forward
+ * (:109-111) in front: h' = bf16(h + delta) (delta NULL: h' = h), x = bf16(weight * bf16(h' * rsqrt(mean(h'^2) +
+ * eps))), statistics in fp32; h' goes to h_out when h_out is not NULL. hidden a multiple of 8 up to 16384,
+ * 16-byte aligned tensors. Replaces: RMSNorm.forward and the residual adds (engine/model.py:24-36, 109-111). */
+int bpt_rms_norm_residual(const void* h, const void* delta, const void* weight, void* h_out, void* x_out,
+                          int64_t rows, int64_t hidden, float eps, int flags, void* stream);
+
+/* One new token per sequence, from the fused q/k/v projection qkv [B, ld] (q heads, then k heads, then v heads,
+ * D = 128 each): q head -> RMSNorm(q_norm) -> rotate-half RoPE(cos, sin [B, D]) -> q_out [B, Hq, D]; k head ->
+ * RMSNorm(k_norm) -> RoPE -> FP8 E4M3 store (x / k_scale, as bpt_paged_kv_write) at slot write_offsets[b] of block
+ * write_blocks[b] of k_pool [num_blocks, block_size, Hkv, D]; v head -> FP8 store to v_pool. Every bf16 rounding
+ * of the reference's tensors is kept. Replaces: Attention.forward's q_norm / k_norm and rope.apply
+ * (engine/model.py:63-70, engine/rope.py:31-43) and the cache write (engine/kv_cache.py:150-161). */
+int bpt_qk_norm_rope_kv_write(const void* qkv, int64_t ld, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                              const void* q_norm, const void* k_norm, const void* cos, const void* sin, float eps,
+                              void* q_out, const int32_t* write_blocks, const int32_t* write_offsets, void* k_pool,
+                              void* v_pool, float k_scale, float v_scale, int64_t block_size, int64_t num_blocks,
+                              int flags, void* stream);
 
 #ifdef __cplusplus
 }

@@ -102,3 +102,86 @@ def test_decode_step_graph_replay_equals_eager():
     assert torch.equal(eager.lengths, graphed.lengths)
     assert torch.equal(eager.tokens, graphed.tokens)
     torch.testing.assert_close(eager.hidden.float(), graphed.hidden.float(), atol=0, rtol=0)
+
+
+def test_fused_rms_norm_residual_matches_reference_ops():
+    from bpt_b200.decode import rms_norm
+    from bpt_b200.kernels.decode_fused import rms_norm_residual
+
+    g = torch.Generator().manual_seed(7)
+    h = (torch.randn(64, 2048, generator=g) * 3).to(torch.bfloat16)
+    delta = torch.randn(64, 2048, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    h_out = torch.empty(64, 2048, dtype=torch.bfloat16, device="cuda")
+    _, x = rms_norm_residual(h.cuda(), w.cuda(), 1e-6, delta=delta.cuda(), h_out=h_out)
+    want_h = h + delta  # the reference's bf16 residual tensor
+    assert torch.equal(h_out.cpu(), want_h)
+    want = rms_norm(want_h, w, 1e-6)  # engine/model.py:32-35 on the CPU
+    got = x.cpu()
+    # the fp32 statistics are summed in another order: at most one bf16 step apart, almost always equal
+    assert (got.float() - want.float()).abs().max() <= 2 ** -7 * want.float().abs().max()
+    assert (got == want).float().mean() > 0.98
+    _, x2 = rms_norm_residual(h.cuda(), w.cuda(), 1e-6)  # no residual
+    assert (x2.cpu().float() - rms_norm(h, w, 1e-6).float()).abs().max() <= 2 ** -7 * 8
+
+
+def test_fused_qk_norm_rope_kv_write_matches_reference_ops():
+    from bpt_b200.decode import random_e4m3_codes, rms_norm, rope_apply, rope_cos_sin
+    from bpt_b200.kernels.decode_fused import qk_norm_rope_kv_write
+    from bpt_b200.kernels.kv_attention import PagedQuantKV
+
+    b, hq, hkv, d = 12, 16, 8, 128
+    g = torch.Generator().manual_seed(11)
+    qkv = torch.randn(b, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    pos = torch.randint(0, 5000, (b,), generator=g)
+    cos, sin = rope_cos_sin(pos, d, 1e6, torch.bfloat16)
+    pages = 4 * b
+    gd = torch.Generator(device="cuda").manual_seed(3)
+    kpool = random_e4m3_codes((pages, 16, hkv, d), gd, "cuda")
+    vpool = random_e4m3_codes((pages, 16, hkv, d), gd, "cuda")
+    table = torch.randperm(pages, generator=g).to(torch.int32).view(b, 4)
+    kv = PagedQuantKV("fp8", kpool, vpool, table.cuda(), 16, 1.0 / 64, 1.0 / 32)
+    wb = table[:, 1].contiguous()
+    wo = torch.randint(0, 16, (b,), generator=g).to(torch.int32)
+    before_k, before_v = kpool.cpu(), vpool.cpu()
+    q_out = torch.empty(b, hq, d, dtype=torch.bfloat16, device="cuda")
+    qk_norm_rope_kv_write(qkv.cuda(), hq, hkv, qn.cuda(), kn.cuda(), cos.cuda(), sin.cuda(), 1e-6, kv, wb.cuda(),
+                          wo.cuda(), q_out=q_out)
+    # the reference on the CPU: engine/model.py:63-70 with rope.apply, then the FP8 store of the paged write
+    q = rope_apply(rms_norm(qkv[:, : hq * d].view(b, hq, d), qn, 1e-6), cos, sin)
+    k = rope_apply(rms_norm(qkv[:, hq * d : (hq + hkv) * d].view(b, hkv, d), kn, 1e-6), cos, sin)
+    v = qkv[:, (hq + hkv) * d :].view(b, hkv, d)
+    got_q = q_out.cpu()
+    assert (got_q.float() - q.float()).abs().max() <= 2 ** -6 * q.float().abs().max()
+    assert (got_q == q).float().mean() > 0.97
+    kp, vp = kpool.cpu(), vpool.cpu()
+    for i in range(b):
+        # v: no float op in front of the store, so its codes are the oracle's bit for bit
+        assert torch.equal(vp[wb[i], wo[i]], okv.fp8_store(v[i].float(), 1.0 / 32))
+        want_k = okv.fp8_store(k[i].float(), 1.0 / 64)
+        got_k = kp[wb[i], wo[i]]
+        assert (got_k == want_k).float().mean() > 0.97  # a norm summed in another order can move a code by one
+        assert (okv.fp8_load(got_k, 1.0 / 64) - okv.fp8_load(want_k, 1.0 / 64)).abs().max() <= 2 ** -3 * k[i].float().abs().max()
+        before_k[wb[i], wo[i]] = got_k
+        before_v[wb[i], wo[i]] = vp[wb[i], wo[i]]
+    assert torch.equal(before_k, kp) and torch.equal(before_v, vp)  # nothing else written
+
+
+def test_fused_decode_step_matches_unfused():
+    from bpt_b200.decode import Qwen3Decoder, Qwen3Dims
+
+    dims = Qwen3Dims(layers=3, intermediate=1024, vocab=512)
+    lengths = torch.tensor([33, 16, 150, 1, 77, 64])
+    plain = Qwen3Decoder(dims, lengths, seed=9, capacity=8, fused=False)
+    fused = Qwen3Decoder(dims, lengths, seed=9, capacity=8, fused=True)
+    for _ in range(2):
+        plain.tokens.copy_(torch.tensor([5, 6, 7, 8, 9, 10]))
+        fused.tokens.copy_(plain.tokens)
+        plain.step()
+        fused.step()
+    torch.cuda.synchronize()
+    a, b = plain.hidden.float(), fused.hidden.float()
+    assert ((a - b).norm() / a.norm()).item() < 2e-2
+    assert torch.equal(plain.lengths, fused.lengths)
