@@ -18,6 +18,7 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_WORKSPACE, ERR_CUDA = range
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 KV_FP8, KV_INT8 = 1, 2
 FLAG_PDL = 1
+FLAG_KV_READY = 2
 
 _DTYPES = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
 

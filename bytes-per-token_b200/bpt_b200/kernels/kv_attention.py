@@ -250,7 +250,9 @@ def attend(
     """Decode attention over a quantized cache: [B, Hq, D] (fp32 unless `out` says otherwise).
 
     Paged caches run one fused launch: the splits of a sequence are merged by the last of its CTAs to finish.
-    KIVI caches run the split kernel, then the merge kernel.
+    KIVI caches run the split kernel, then the merge kernel. `pdl=True` launches with programmatic dependent
+    launch; `kv_ready=True` adds the promise that the lengths, block table and pools are not written by the
+    kernel this call follows, so the persistent kernel starts copying pages before it waits on that kernel.
     """
     if not isinstance(kv, PagedQuantKV):
         merged = merge_partials(*decode_attention(q, kv, lengths, scale, **launch))
@@ -278,7 +280,8 @@ def attend(
         ptr(q), dtype_code(q.dtype), q.stride(0), q.stride(1), ptr(kv.k_pool), ptr(kv.v_pool), code, ks, vs, ptr(kss),
         ptr(vss), ptr(kv.block_table), kv.block_table.stride(0), ptr(lengths), b, hq, hkv, d, bs, nb, split, n_splits,
         float(scale), ptr(out), dtype_code(out.dtype), ptr(workspace), workspace.numel(),
-        _lib.FLAG_PDL if launch.get("pdl") else 0, stream_of(device))
+        (_lib.FLAG_PDL if launch.get("pdl") else 0) | (_lib.FLAG_KV_READY if launch.get("kv_ready") else 0),
+        stream_of(device))
     check(st, "attend (paged)")
     return out
 

@@ -63,6 +63,7 @@ struct PagedArgs {
   int scale_bytes;  // kBS * Hkv * 2 (INT8) or 0
   int nst;          // pipeline stages
   // persistent kernel
+  int early;          // BPT_FLAG_KV_READY under PDL: map the pages and copy them before waiting on the predecessor
   int persist_ctas;   // CTAs (one per SM)
   int max_cta_pages;  // capacity of a CTA's page list
 };

@@ -470,7 +470,9 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
   float* ptile = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(misc + 3) + 15) & ~uintptr_t(15));
 
   pdl_launch_dependents();
-  pdl_wait();
+  // Under BPT_FLAG_KV_READY the lengths, block table and pools are final already: the prologue and the first
+  // stages' page copies run while the previous kernel finishes; q, the output and the workspace wait for it.
+  if (!a.early) pdl_wait();
 
   // ---- prologue: offsets, this CTA's range, its pages' blocks ----
   for (int b = tid; b < B; b += blockDim.x) {
@@ -521,20 +523,35 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
     plp[k] = lp;
     pblk[k] = a.block_table[(int64_t)lo * a.bt_stride + lp];
   }
-  // A sequence with no tokens is in nobody's range and gets a zero output: sequence b from CTA b mod G, one warp each.
-  for (int b = cta + G * warp; b < B; b += G * (blockDim.x >> 5))
-    if (off[b + 1] == off[b])
-      for (int i = lane; i < a.Hq * D; i += 32) out_store(a.out, a.out_dtype, (int64_t)b * a.Hq * D + i, 0.f);
   __syncthreads();
+  const bool producer = warp == Hkv;
+  // A sequence with no tokens is in nobody's range and gets a zero output: sequence b from CTA b mod G, one warp
+  // each (the consumer warps; every warp of a CTA without pages), after the wait on the previous kernel.
+  if (!producer || n <= 0) {
+    if (a.early) pdl_wait();
+    const int nw = n <= 0 ? int(blockDim.x >> 5) : Hkv;
+    for (int b = cta + G * warp; b < B; b += G * nw)
+      if (off[b + 1] == off[b])
+        for (int i = lane; i < a.Hq * D; i += 32) out_store(a.out, a.out_dtype, (int64_t)b * a.Hq * D + i, 0.f);
+  }
   if (n <= 0) return;
 
-  const bool producer = warp == Hkv;
   if (producer) {
     // ---------------- producer warp ----------------
     const uint64_t policy = l2_policy_evict_first();
+    // Early start: pages 0 .. pre - 1 are requested before the wait on the previous kernel, their q copies after it.
+    const int pre = a.early ? min(n, a.nst) : 0;
+    auto q_copies_of_first_pages = [&]() {
+      pdl_wait();
+      for (int k = 0; k < pre; ++k)
+        if ((k == 0 || pseq[k - 1] != pseq[k]) && lane == 3)
+          bulk_g2s(stages + k * lay.stage_bytes + lay.q_off,
+                   static_cast<const uint8_t*>(a.q) + (int64_t)pseq[k] * lay.q_bytes, lay.q_bytes, &full[k]);
+    };
     int st = 0;        // stage of page k
     uint32_t eph = 1;  // parity of the empty phase that frees it: (k / nst - 1) & 1
     for (int k = 0; k < n; ++k, st = (st + 1 == a.nst) ? 0 : st + 1, eph ^= (st == 0) ? 1u : 0u) {
+      if (k == pre && pre > 0) q_copies_of_first_pages();
       if (misc[2]) break;
       if (k >= a.nst && !mbar_wait_warp(&empty[st], eph)) {
         misc[2] = 1;
@@ -575,11 +592,12 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
                      reinterpret_cast<const uint8_t*>(a.v_scales) + (int64_t)blk * a.scale_bytes, a.scale_bytes, &full[st]);
         }
       }
-      if (first && lane == 3)
+      if (first && lane == 3 && k >= pre)
         bulk_g2s(base + lay.q_off, static_cast<const uint8_t*>(a.q) + (int64_t)b * lay.q_bytes, lay.q_bytes, &full[st]);
       __syncwarp();
       if (lane == 0) misc[1] = k + 1;
     }
+    if (pre == n && pre > 0) q_copies_of_first_pages();  // every page fitted in the first stages
     return;
   }
 
@@ -878,6 +896,7 @@ PersistKernel persist_kernel() {
 template <int D, int REP, int KIND>
 int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   PagedArgs a = a0;
+  a.early = (flags & BPT_FLAG_PDL) && (flags & BPT_FLAG_KV_READY) ? 1 : 0;
   const int q_esize = a.q_dtype == BPT_DTYPE_F32 ? 4 : 2;
   const PersistLayout lay = persist_layout<D, 0>(a.Hkv, a.Hq, q_esize, a.scale_bytes);
   const int G = a.persist_ctas;

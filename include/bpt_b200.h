@@ -46,6 +46,10 @@ extern "C" {
 
 /* launch flags */
 #define BPT_FLAG_PDL 1 /* launch with programmatic dependent launch (prologue overlaps the previous kernel) */
+/* With BPT_FLAG_PDL, for the paged attention: the caller promises that the lengths, the block table and the KV
+ * pools are not written by the kernel this launch follows, so the kernel maps its pages and starts their copies
+ * before it waits on that kernel (q, the output and the workspace are still touched only after the wait). */
+#define BPT_FLAG_KV_READY 2
 
 int bpt_abi_version(void);
 const char* bpt_last_error(void);

@@ -88,6 +88,29 @@ def test_paged_attend_fused_merge_matches_oracle(kind, batch, hq, hkv, d, length
         assert bf[lengths.index(0)].abs().sum() == 0  # no tokens: zeros, not NaN
 
 
+@pytest.mark.parametrize("kind", ["fp8", "int8"])
+@pytest.mark.parametrize("batch,hq,hkv,d,lengths", [CASES[0], CASES[1], (3, 16, 8, 128, [5000, 0, 2049])])
+def test_early_start_under_pdl_matches_plain(kind, batch, hq, hkv, d, lengths):
+    # kv_ready: pages are mapped and copied before the wait on the previous kernel (q, out and the workspace
+    # after it); a chain of such calls (the previous one writing the same out and workspace) equals plain calls,
+    # with empty sequences, pages that all fit the first stages, and long sequences that refill the stages
+    from bpt_b200.kernels.kv_attention import attend
+
+    case = small_case(kind, batch, hq, hkv, d, lengths, seed=3 + d)
+    scale = 1 / math.sqrt(d)
+    want = attend(case.q, case.kv, case.lengths, scale)
+    other = small_case(kind, batch, hq, hkv, d, lengths, seed=99)
+    out = torch.full((batch, hq, d), float("nan"), device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            attend(other.q, other.kv, other.lengths, scale, out=out, pdl=True, kv_ready=True)
+            attend(case.q, case.kv, case.lengths, scale, out=out, pdl=True, kv_ready=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    close(out.cpu(), oatt.paged_attend(case.q.cpu(), to_oracle(case.kv), case.lengths.cpu(), scale))
+
+
 def test_config2_full_size_against_oracle():
     from bpt_b200 import workloads
     from bpt_b200.kernels.kv_attention import attend
