@@ -1,12 +1,15 @@
 // W4A16 linear for M <= 8 tokens as a persistent streaming GEMV: y[M, N] = x[M, K] . (scale * (q - zero))^T.
 //
-// At most one CTA per SM. CTA b owns the contiguous 16-row weight tiles [b T / P, (b + 1) T / P). A producer
-// warp streams each tile (16 code rows, the tile's fp16 scales and zero-point words) into a ring of shared-memory
-// stages with bulk copies (TMA engine), all issued before the kernel waits on its predecessor: the weights do not
-// depend on it. The CTA asks for at most ~113 KB of shared memory and ~32 K registers, so under programmatic
-// dependent launch the next call's CTAs sit beside this one's and fetch their weights while this one computes.
-// Eight consumer warps split K by whole groups; each keeps its groups' x in registers and runs them against every
-// tile of the CTA, so x is read once per CTA and the tiles' code words are the only shared-memory traffic.
+// At most one CTA per SM. CTA b owns the contiguous 16-row weight tiles [b T / P, (b + 1) T / P). Thread 0
+// streams each tile (16 code rows, the tile's fp16 scales and zero-point words) into a ring of shared-memory
+// stages with bulk copies (TMA engine): the first ring-full right after the CTA lets its dependents launch and
+// before the kernel waits on its predecessor (the weights do not depend on it), each later tile as soon as the
+// chunk of tiles that held its stage has been reduced. The CTA asks for at most ~113 KB of shared memory and
+// ~29 K registers, so under programmatic dependent launch the next call's CTAs sit beside this one's and fetch
+// their weights while this one computes. Eight warps split K by whole groups; each keeps its groups' x in
+// registers and runs them against every tile of the CTA, so x is read once per CTA and the tiles' code words
+// are the only shared-memory traffic. (A dedicated copy warp made nine warps, which capped the registers at 96
+// per thread for two CTAs per SM, and measured slower.)
 //
 // mma.sync m16n8k16 bf16 -> fp32 with the WEIGHTS as A (the 16 rows of a tile) and the tokens as B (up to 8
 // columns). K is walked in blocks of 64 inputs (4 k-steps u = 0..3). In a block, lane (g, c) owns code words
@@ -24,8 +27,8 @@ namespace bpt {
 namespace {
 
 constexpr int kRows = 16;                        // weight rows per tile (the MMA's M)
-constexpr int kConsumers = 8;                    // consumer warps (K split), two per SM sub-partition
-constexpr int kThreads = 32 * (kConsumers + 1);  // + the producer warp
+constexpr int kConsumers = 8;                    // warps (K split), two per SM sub-partition
+constexpr int kThreads = 32 * kConsumers;        // thread 0 also issues the tiles' copies
 constexpr int kMaxTok = 8;                       // tokens per launch (the MMA's N)
 constexpr int kChunk = 3;                        // tiles a warp holds partial sums for at once
 constexpr int kBudgetShared = 113 * 1024;        // two CTAs per SM (this call's and the next one's)
@@ -52,13 +55,13 @@ struct StreamLayout {
   int ring, red, bars, total;
 };
 
-// ring [ns][stage] | partial sums [2][chunk tiles][warps][16 rows][M] f32 | mbarriers full[ns], empty[ns]
+// ring [ns][stage] | partial sums [2][chunk tiles][warps][16 rows][M] f32 | mbarriers full[ns]
 __host__ __device__ inline StreamLayout stream_layout(int M, int stage, int ns) {
   StreamLayout l;
   l.ring = 0;
   l.red = ns * stage;
   l.bars = l.red + ((2 * kChunk * kConsumers * kRows * M * 4 + 15) & ~15);
-  l.total = l.bars + 2 * ns * 8;
+  l.total = l.bars + ns * 8;
   return l;
 }
 
@@ -94,40 +97,31 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
   uint8_t* ring = smem + L.ring;
   float* red = reinterpret_cast<float*>(smem + L.red);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + a.ns;
 
+  // tile j's copies into stage j mod ns, completing on full[stage]
+  const uint64_t policy = l2_policy_evict_first();
+  auto issue_tile = [&](int j) {
+    const int s = j % a.ns;
+    const int row_bytes = a.K >> 1;
+    uint8_t* st = ring + s * a.stage;
+    const int64_t row0 = int64_t(tb + j) * kRows;
+    mbar_arrive_expect_tx(&full[s], uint32_t(kRows * row_bytes + a.sbytes + a.zbytes));
+    for (int r = 0; r < kRows; ++r)
+      bulk_g2s_evict_first(st + r * a.pitch, a.qweight + (row0 + r) * row_bytes, uint32_t(row_bytes), &full[s],
+                           policy);
+    bulk_g2s(st + kRows * a.pitch, a.scales + row0 * a.G, uint32_t(a.sbytes), &full[s]);
+    if (a.zbytes) bulk_g2s(st + kRows * a.pitch + a.sbytes, a.qzeros + row0 * a.ZW, uint32_t(a.zbytes), &full[s]);
+  };
   if (tid == 0) {
-    for (int s = 0; s < a.ns; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumers);
-    }
+    for (int s = 0; s < a.ns; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
   pdl_launch_dependents();  // the next call may now place its CTAs beside this one and fetch its weights
+  if (tid == 0)  // after the trigger: ~18 copies a tile would otherwise hold back the next call's launch
+    for (int j = 0; j < min(nt, a.ns); ++j) issue_tile(j);
 
-  if (warp == 0) {  // producer: every tile's copies, refilling a stage once the consumers release it
-    if (lane == 0) {
-      const uint64_t policy = l2_policy_evict_first();
-      const int row_bytes = a.K >> 1;
-      const uint32_t tx = uint32_t(kRows * row_bytes + a.sbytes + a.zbytes);
-      for (int j = 0; j < nt; ++j) {
-        const int s = j % a.ns;
-        if (j >= a.ns && !mbar_wait_sleep(&empty[s], uint32_t((j / a.ns - 1) & 1), 64u)) break;
-        uint8_t* st = ring + s * a.stage;
-        const int64_t row0 = int64_t(tb + j) * kRows;
-        mbar_arrive_expect_tx(&full[s], tx);
-        for (int r = 0; r < kRows; ++r)
-          bulk_g2s_evict_first(st + r * a.pitch, a.qweight + (row0 + r) * row_bytes, uint32_t(row_bytes), &full[s],
-                               policy);
-        bulk_g2s(st + kRows * a.pitch, a.scales + row0 * a.G, uint32_t(a.sbytes), &full[s]);
-        if (a.zbytes) bulk_g2s(st + kRows * a.pitch + a.sbytes, a.qzeros + row0 * a.ZW, uint32_t(a.zbytes), &full[s]);
-      }
-    }
-    return;  // the consumers wait for every copy before the CTA exits
-  }
-
-  const int cw = warp - 1, ctid = tid - 32;
+  const int cw = warp, ctid = tid;
   const int g = lane >> 2, c = lane & 3;
   const int gb = cw * a.G / kConsumers, ge = (cw + 1) * a.G / kConsumers;  // this warp's groups
   constexpr int group = SPG * 16;
@@ -216,11 +210,6 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
         }
       }
     }
-    __syncwarp();
-    if (lane == 0)
-#pragma unroll
-      for (int jj = 0; jj < kChunk; ++jj)  // done with these stages (even on a timeout)
-        if (j0 + jj < j1) mbar_arrive(&empty[(j0 + jj) % a.ns]);
     // the chunk's partials in red[chunk parity][tile][warp][row][token] (the next chunk uses the other half), one
     // barrier, then each (tile, token, row) item is summed over the warps in a fixed order
     float* rc = red + ((j0 / chunk) & 1) * (kChunk * kConsumers * kRows * a.M);
@@ -238,6 +227,8 @@ __global__ void __launch_bounds__(kThreads, 2) w4a16_stream_kernel(const StreamA
       }
     }
     consumers_sync();
+    if (tid == 0 && ok)  // every warp is past its reads of the chunk's stages: the tiles ns further on go there
+      for (int j = j0 + a.ns; j < min(nt, j1 + a.ns); ++j) issue_tile(j);
     if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output row0 / 2 + p
       for (int i = ctid; i < (j1 - j0) * a.M * (kRows / 2); i += 32 * kConsumers) {
         const int jj = i / (a.M * (kRows / 2)), rest = i - jj * (a.M * (kRows / 2));
