@@ -12,6 +12,9 @@ dequantize, attend) on the host cores, on a bounded sample of the same workload.
 
 Inputs larger than L2: the GEMV rotates over 40 weight copies (262 MB) and the attention over 3 batches with
 their own pools (about 450 MB of KV touched per cycle), so no step finds its data in the 126 MB L2.
+
+`kernels.rms_norm_int8` times the next row past the path in its own region (RMSNorm + per-token INT8 of
+[16384, 2048] bf16 rows, three rotating inputs of 64 MB), with the reference's CPU definition beside it at N=1.
 """
 
 from __future__ import annotations
@@ -38,6 +41,12 @@ WORKLOAD = ("config1 W4A16 GEMV (M=1, K=2048, N=6144, asym INT4 g128) + config2 
             "(B=32, 16 Q / 8 KV heads, D=128, lengths U[512,4096], page 16, 16384-page pool)")
 GEMV_COPIES = 40
 ATTN_BATCHES = 3
+NQ_ROWS, NQ_D, NQ_COPIES = 16384, 2048, 3  # rms_norm_int8: 3 x 64 MB of bf16 rows rotate (above L2)
+
+
+def norm_quant_bytes(rows: int, d: int, residual: bool) -> int:
+    """rms_norm_int8's algorithmic bytes: bf16 x read, int8 codes and fp32 scales written, the weight once."""
+    return rows * d * 3 + rows * 4 + d * 2 + (4 * rows * d if residual else 0)
 PROFILE_SUMMARY = ROOT / "profiles" / "paged_attention_fp8_config2.md"
 
 
@@ -244,6 +253,24 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         gemv_total_ms = timed(gemv)
     gemv_ms = [gemv_total_ms / args.steps]
     attn_ms = [attn_total_ms / args.steps]
+
+    # the next row past the path: RMSNorm + per-token INT8 on [NQ_ROWS, NQ_D] bf16, rotating over NQ_COPIES inputs
+    # (larger than L2 together), programmatic dependent launch
+    from bpt_b200.kernels.norm_quant import rms_norm_int8
+
+    gq = torch.Generator(device=device).manual_seed(1000 + rank)
+    nq_x = [(torch.randn(NQ_ROWS, NQ_D, generator=gq, device=device) * 3).to(torch.bfloat16) for _ in range(NQ_COPIES)]
+    nq_w = (torch.rand(NQ_D, generator=gq, device=device) + 0.5).to(torch.bfloat16)
+    nq_out = [(torch.empty(NQ_ROWS, NQ_D, dtype=torch.int8, device=device), torch.empty(NQ_ROWS, device=device))
+              for _ in range(NQ_COPIES)]
+
+    def norm_quant(i: int):
+        rms_norm_int8(nq_x[i % NQ_COPIES], nq_w, 1e-6, out=nq_out[i % NQ_COPIES], pdl=True)
+
+    for i in range(3):
+        norm_quant(i)
+    nq_ms = [timed(norm_quant) / args.steps]
+    del nq_x, nq_out
     my_bytes = sum(gemv_bytes + attn_bytes[k % ATTN_BATCHES] for k in range(args.steps))
 
     # end to end: the public API with host buffers, the step's inputs H2D and results D2H inside the region
@@ -288,6 +315,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "bytes": my_bytes,
         "gemv_ms": gemv_ms,
         "attn_ms": attn_ms,
+        "nq_ms": nq_ms,
         "clocks": sampler.summary(),
     }
     del weights, attn, pin
@@ -305,6 +333,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     peak, peak_kind = measured_peaks()
     attn_avg_ms = statistics.fmean(gathered[0]["attn_ms"])
     gemv_avg_ms = statistics.fmean(gathered[0]["gemv_ms"])
+    nq_avg_ms = statistics.fmean(gathered[0]["nq_ms"])
+    nq_bytes = norm_quant_bytes(NQ_ROWS, NQ_D, False)
     attn_bytes_avg = statistics.fmean(attn_bytes)
     achieved = attn_bytes_avg / (attn_avg_ms * 1e-3) / 1e9
     traffic = profiled_traffic()
@@ -339,6 +369,10 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
                            "bytes": gemv_bytes},
             "paged_attention_fp8": {"us_per_call": round(attn_avg_ms * 1e3, 2), "gbs": round(achieved, 1),
                                     "frac_of_peak": round(achieved / peak, 3), "bytes": round(attn_bytes_avg)},
+            "rms_norm_int8": {"shape": f"[{NQ_ROWS}, {NQ_D}] bf16 -> int8 + fp32 scale per row",
+                              "us_per_call": round(nq_avg_ms * 1e3, 2),
+                              "gbs": round(nq_bytes / (nq_avg_ms * 1e-3) / 1e9, 1),
+                              "frac_of_peak": round(nq_bytes / (nq_avg_ms * 1e-3) / 1e9 / peak, 3), "bytes": nq_bytes},
         },
         "roofline": {
             "kernel": "paged_attn_persistent_kernel<128, 2, FP8> (fused split merge)",
@@ -372,6 +406,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         }
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(sample_seqs=4)
+        line["kernels"]["rms_norm_int8"]["cpu_baseline"] = norm_quant_cpu_baseline()
     return line
 
 
@@ -455,6 +490,25 @@ def cpu_baseline(sample_seqs: int = 4, repeats: int = 3) -> dict:
                   f"({int(lengths.sum())} tokens); median of {repeats}",
         "s_per_sample": round(t, 4),
     }
+
+
+def norm_quant_cpu_baseline(repeats: int = 3) -> dict:
+    """The reference's definition of rms_norm_int8 (kernels/reference.py:44-55, restated by the oracle) on the
+    host cores, on the bench's [NQ_ROWS, NQ_D] bf16 shape: one full call, median of `repeats`."""
+    from oracle import norm_quant as onq
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1000)
+    x = (torch.randn(NQ_ROWS, NQ_D, generator=g) * 3).to(torch.bfloat16)
+    w = (torch.rand(NQ_D, generator=g) + 0.5).to(torch.bfloat16)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        onq.rms_norm_int8(x, w, 1e-6)
+        times.append(time.perf_counter() - t0)
+    s = statistics.median(times)
+    return {"us_per_call": round(s * 1e6, 1), "gbs": round(norm_quant_bytes(NQ_ROWS, NQ_D, False) / s / 1e9, 2),
+            "cores": torch.get_num_threads(), "kind": "port", "sample": "one full call, median of 3"}
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, list] = {
     "bpt_rms_norm_residual": [P, P, P, P, P, I64, I64, F32, I32, P],
     "bpt_qk_norm_rope_kv_write": [P, I64, I64, I64, I64, I64, P, P, P, P, F32, P, P, P, P, P, F32, F32, I64, I64, I32,
                                   P],
+    "bpt_rms_norm_int8": [P, I32, I64, P, I32, P, P, P, P, I64, I64, F32, I32, P],
     "bpt_w4a16_quantize": [P, I32, I64, I64, I64, P, P, P, P],
     "bpt_paged_decode_partials": [P, I32, I64, I64, P, P, I32, F32, F32, P, P, P, I64, P, I64, I64, I64, I64, I64, I64,
                                   I64, I64, F32, P, P, I32, P],

@@ -228,6 +228,18 @@ int bpt_qk_norm_rope_kv_write(const void* qkv, int64_t ld, int64_t B, int64_t Hq
                               void* v_pool, float k_scale, float v_scale, int64_t block_size, int64_t num_blocks,
                               int flags, void* stream);
 
+/* RMSNorm fused with per-token symmetric INT8 quantization (the activation quantizer before a W8A8 linear):
+ * for every row of x [rows, d] (x_dtype, row stride x_row_stride elements, unit inner stride) and weight [d]
+ * (w_dtype), in fp32: y = x * (1 / sqrt(sum(x^2) / d + eps)) * weight, scale[row] = max(max|y| / 127, 1e-12),
+ * codes[row] = clamp(rint(y / scale), -128, 127) -> codes int8 [rows, d] contiguous, scale float32 [rows].
+ * delta (NULL for none): x + delta, rounded to x_dtype, is normalized instead and goes to x_out (NULL: not
+ * written); delta and x_out are contiguous [rows, d] in x_dtype. Any d >= 1; 16-byte vector accesses when
+ * alignment allows. Replaces: kernels/norm_quant.py:72-109 (rms_norm_int8, its Triton kernel :42-67), defined
+ * by kernels/reference.py:44-55; with delta, also the residual add of engine/model.py:109-111. */
+int bpt_rms_norm_int8(const void* x, int x_dtype, int64_t x_row_stride, const void* weight, int w_dtype,
+                      const void* delta, void* x_out, void* codes, void* scale, int64_t rows, int64_t d, float eps,
+                      int flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

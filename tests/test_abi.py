@@ -64,3 +64,9 @@ def test_host_side_validation_runs_before_any_launch(library):
     st = L.bpt_paged_kv_write(1, 1, 2, 0, 0, 0, 1, 1, 1, 96, 1, 1, 1, 1, 1, 1.0, 1.0, None, None, 16, 1, None)
     assert st == _lib.ERR_UNSUPPORTED and b"D=96" in L.bpt_last_error()
     assert L.bpt_paged_attend_workspace_bytes(32, 16, 128, 8) >= 32 * 8 * 16 * 128 * 4
+    # rms_norm_int8: x_out without delta, and a row stride shorter than the row
+    assert L.bpt_rms_norm_int8(None, 2, 64, None, 2, None, None, None, None, 0, 64, 1e-6, 0, None) == _lib.OK  # empty
+    st = L.bpt_rms_norm_int8(1, 2, 64, 1, 2, None, 1, 1, 1, 4, 64, 1e-6, 0, None)
+    assert st == _lib.ERR_INVALID and b"needs delta" in L.bpt_last_error()
+    st = L.bpt_rms_norm_int8(1, 2, 32, 1, 2, None, None, 1, 1, 4, 64, 1e-6, 0, None)
+    assert st == _lib.ERR_INVALID and b"row stride" in L.bpt_last_error()

@@ -194,3 +194,54 @@ def test_default_split_golden_values(golden):
     g = golden["default_split"]
     for case, want in zip(g["cases"].tolist(), g["split"].tolist(), strict=True):
         assert default_split(*case) == want
+
+
+# ---- RMSNorm + per-token INT8 (kernel 1) ------------------------------------------------------------------------
+
+
+@pytest.fixture(scope="module")
+def norm_golden():
+    from conftest import GOLDEN
+
+    return torch.load(GOLDEN.with_name("norm_quant.pt"), weights_only=True)
+
+
+@pytest.mark.parametrize("name", ["kat", "f32_zero_row", "bf16_3d", "f16_2048", "bf16_x_f32_w", "residual"])
+def test_rms_norm_int8_restatement_matches_reference(norm_golden, name):
+    """The oracle against reference.rms_norm_int8 (made by tests/golden/make_golden_norm_quant.py): scales within
+    FLOAT_ORDER (the row's mean is a host-BLAS sum), codes bit-exact except a code at a rounding tie."""
+    from oracle import norm_quant as onq
+
+    g = norm_golden[name]
+    if name == "residual":
+        h, codes, scale = onq.add_rms_norm_int8(g["h"], g["delta"], g["weight"], float(g["eps"]))
+        assert h.dtype == torch.bfloat16 and torch.equal(h, g["x"])
+    else:
+        codes, scale = onq.rms_norm_int8(g["x"], g["weight"], float(g["eps"]))
+    assert codes.dtype == torch.int8 and codes.shape == g["codes"].shape and scale.shape == g["scale"].shape
+    torch.testing.assert_close(scale, g["scale"], **FLOAT_ORDER)
+    diff = (codes.int() - g["codes"].int()).abs()
+    assert diff.max() <= 1 and (diff > 0).float().mean() < 1e-3
+
+
+def test_rms_norm_int8_known_values(norm_golden):
+    """reference tests/kernels/test_reference.py:27-31: y = x / 2.5, scale 1.6 / 127, codes [95, -127, 0, 0]."""
+    from oracle import norm_quant as onq
+
+    codes, scale = onq.rms_norm_int8(torch.tensor([[3.0, -4.0, 0.0, 0.0]]), torch.ones(4), 0.0)
+    assert codes.tolist() == [[95, -127, 0, 0]] == norm_golden["kat"]["codes"].tolist()
+    assert scale.item() == pytest.approx(1.6 / 127)
+
+
+def test_rms_norm_int8_is_the_model_norm_within_half_a_step(norm_golden):
+    """reference tests/kernels/test_reference.py:34-55: codes * scale is the model's RMSNorm within half a step;
+    an all-zero token gets zero codes and a finite scale; every other token uses its whole range."""
+    from oracle import norm_quant as onq
+
+    g = norm_golden["bf16_3d"]
+    codes, scale = onq.rms_norm_int8(g["x"], g["weight"], float(g["eps"]))
+    assert ((onq.dequantize_int8(codes, scale) - g["model_norm"]).abs() <= scale / 2 + 1e-5).all()
+    z = norm_golden["f32_zero_row"]
+    codes, scale = onq.rms_norm_int8(z["x"], z["weight"], float(z["eps"]))
+    assert codes[4].abs().sum() == 0 and torch.isfinite(scale).all() and scale[4].item() == pytest.approx(1e-12)
+    assert codes.abs().amax(-1)[torch.arange(9) != 4].eq(127).all()
