@@ -11,12 +11,13 @@
 // The row is read once: its elements stay in registers (16-byte loads when the row, the weight and the strides
 // allow it, else one element at a time) and the three passes (sum of squares, max of |y|, the codes) run on that
 // copy. Two launch shapes:
-// - rows of up to 512 chunks (4,096 16-bit or 2,048 fp32 elements; 512 on the one-element path): one WARP per
-//   row, eight rows per CTA, reductions by shuffles only. A row is a few KB, so an SM needs many rows in flight
-//   to cover HBM latency: small register footprints (the row kept as packed 16-byte words) and no block barrier
-//   let ~16-32 rows per SM load at once.
-// - longer rows: one CTA per row (up to 256 threads); a row longer than the CTA's registers hold (more than
-//   16,384 16-bit or 8,192 fp32 elements) reads its remainder again, from L2.
+// - 512 rows or more, each of up to 512 chunks (4,096 16-bit or 2,048 fp32 elements; 512 on the one-element
+//   path): one WARP per row, eight rows per CTA, warps persistent over rows, reductions by shuffles only. A row
+//   is a few KB, so an SM needs many rows in flight to cover HBM latency: the row is kept as packed 16-byte
+//   words, there is no block barrier, and the arithmetic runs two elements per instruction on the packed fp32
+//   pipe (the kernel is otherwise instruction-bound: ~20 operations per element).
+// - fewer or longer rows: one CTA per row (up to 256 threads); a row longer than the CTA's registers hold (more
+//   than 16,384 16-bit or 8,192 fp32 elements) reads its remainder again, from L2.
 // Divisions and the square root are IEEE-rounded, as the reference's fp32 tensor ops are, so results differ from
 // it only through the order of the row's sums.
 #include "common.cuh"
@@ -93,6 +94,40 @@ __device__ __forceinline__ int8_t to_code(float v) {
   int r;
   asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(v));
   return int8_t(r);
+}
+
+// Pairs of fp32 lanes on the packed two-wide fp32 pipe of sm_100 (add/mul/fma .f32x2): each half rounds exactly
+// as the scalar instruction would.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// four codes clamp(rint(v), -128, 127), v0 in the lowest byte: round to nearest even into s32, then two
+// saturating packs (each puts its two values in the low bytes above the third operand's bits)
+__device__ __forceinline__ uint32_t to_codes4(float v0, float v1, float v2, float v3) {
+  int i0, i1, i2, i3;
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(i0) : "f"(v0));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(i1) : "f"(v1));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(i2) : "f"(v2));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(i3) : "f"(v3));
+  uint32_t hi, w;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(i3), "r"(i2), "r"(0));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(i1), "r"(i0), "r"(hi));
+  return w;
 }
 
 __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
@@ -290,6 +325,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCta, 2) rms_norm_int8_rows_kernel
     }
   }
   float ss = 0.f;
+  uint64_t ss2 = pk2(0.f, 0.f);  // the vector path sums even and odd elements apart, then adds the two
 #pragma unroll
   for (int i = 0; i < NPER; ++i) {
     const int ci = lane + 32 * i;
@@ -306,20 +342,38 @@ __global__ void __launch_bounds__(32 * kRowsPerCta, 2) rms_norm_int8_rows_kernel
         else raw[i] = v[0];
         if (xo) store_chunk<T, CH>(xo + int64_t(ci) * CH, v);
       }
+      if constexpr (kVec) {
 #pragma unroll
-      for (int k = 0; k < CH; ++k) ss = fmaf(v[k], v[k], ss);
+        for (int k = 0; k < CH; k += 2) {
+          const uint64_t v2 = pk2(v[k], v[k + 1]);
+          ss2 = fma2(v2, v2, ss2);
+        }
+      } else {
+        ss = fmaf(v[0], v[0], ss);
+      }
     }
+  }
+  if constexpr (kVec) {
+    float s0, s1;
+    upk2(ss2, s0, s1);
+    ss = s0 + s1;
   }
   const float ms = __fdiv_rn(warp_sum(ss), float(d));
   const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+  const uint64_t inv2 = pk2(inv, inv);
 
   auto norm = [&](int i, int ci, float (&y)[CH]) {
     float v[CH], wv[CH];
     if constexpr (kVec) unpack16<T>(raw[i], v);
     else v[0] = raw[i];
     load_weight<CH>(a.weight, w_dtype, int64_t(ci) * CH, wv);
+    if constexpr (kVec) {
 #pragma unroll
-    for (int k = 0; k < CH; ++k) y[k] = __fmul_rn(__fmul_rn(v[k], inv), wv[k]);
+      for (int k = 0; k < CH; k += 2)
+        upk2(mul2(mul2(pk2(v[k], v[k + 1]), inv2), pk2(wv[k], wv[k + 1])), y[k], y[k + 1]);
+    } else {
+      y[0] = __fmul_rn(__fmul_rn(v[0], inv), wv[0]);
+    }
   };
   // up to 64 values in 8 chunks a lane, y stays in registers for the codes (the packed row dies as it forms);
   // longer rows form it again
@@ -338,6 +392,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCta, 2) rms_norm_int8_rows_kernel
   }
   const float scale = fmaxf(__fdiv_rn(warp_max(amax), 127.f), 1e-12f);
   const float rscale = __frcp_rn(scale);
+  const uint64_t r2 = pk2(rscale, rscale), nb2 = pk2(-scale, -scale);
   if (lane == 0) a.scale[row] = scale;
   int8_t* cr = a.codes + row * int64_t(d);
 #pragma unroll
@@ -346,12 +401,22 @@ __global__ void __launch_bounds__(32 * kRowsPerCta, 2) rms_norm_int8_rows_kernel
     if (ci < nchunks) {
       float (&y)[CH] = yv[kKeepY ? i : 0];
       if constexpr (!kKeepY) norm(i, ci, y);
-      alignas(8) int8_t q[CH];
+      if constexpr (kVec) {  // div_by two at a time: q = y r, e = y - q b, q + e r
+        float t[CH];
 #pragma unroll
-      for (int k = 0; k < CH; ++k) q[k] = to_code(div_by(y[k], scale, rscale));
-      if constexpr (CH == 8) *reinterpret_cast<uint2*>(cr + int64_t(ci) * CH) = *reinterpret_cast<const uint2*>(q);
-      else if constexpr (CH == 4) *reinterpret_cast<uint32_t*>(cr + int64_t(ci) * CH) = *reinterpret_cast<const uint32_t*>(q);
-      else cr[ci] = q[0];
+        for (int k = 0; k < CH; k += 2) {
+          const uint64_t y2 = pk2(y[k], y[k + 1]);
+          const uint64_t q2 = mul2(y2, r2);
+          upk2(fma2(fma2(q2, nb2, y2), r2, q2), t[k], t[k + 1]);
+        }
+        uint32_t w[CH / 4];
+#pragma unroll
+        for (int k = 0; k < CH / 4; ++k) w[k] = to_codes4(t[4 * k], t[4 * k + 1], t[4 * k + 2], t[4 * k + 3]);
+        if constexpr (CH == 8) *reinterpret_cast<uint2*>(cr + int64_t(ci) * CH) = make_uint2(w[0], w[1]);
+        else *reinterpret_cast<uint32_t*>(cr + int64_t(ci) * CH) = w[0];
+      } else {
+        cr[ci] = to_code(div_by(y[0], scale, rscale));
+      }
     }
   }
   }  // rows
@@ -383,7 +448,7 @@ int launch_rows_t(const NormQuantArgs& a, int64_t rows, int w_dtype, int flags, 
 }
 
 constexpr int kWarpMaxChunks = 32 * 16;  // the warp-per-row kernel's longest row, in chunks
-constexpr int64_t kWarpMinRows = 1024;   // below this a CTA per row finishes sooner (more SMs share a call)
+constexpr int64_t kWarpMinRows = 512;    // below this a CTA per row finishes sooner (more SMs share a call)
 
 template <typename T, int CH>
 int launch_rows(const NormQuantArgs& a, int64_t rows, int w_dtype, int flags, cudaStream_t stream) {

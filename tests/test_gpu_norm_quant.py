@@ -130,7 +130,7 @@ def test_rms_norm_int8_rejects_bad_buffers():
     (2048, 2048, torch.bfloat16, True),    # the residual add on the warp-per-row shape
 ])
 def test_rms_norm_int8_warp_per_row_shapes(rows, d, dtype, residual):
-    """From 1,024 rows on, a warp takes a row (persistent warps, eight rows a CTA)."""
+    """From 512 rows on, a warp takes a row (persistent warps, eight rows a CTA)."""
     from bpt_b200.kernels.norm_quant import rms_norm_int8
 
     x = rand(rows, d, seed=rows + d, dtype=dtype) * 3
