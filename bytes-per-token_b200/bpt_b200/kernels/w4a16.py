@@ -13,7 +13,9 @@ Format (see include/bpt_b200.h):
 
 The swap into a model follows the reference's module-swap seam (`src/fastserve/quant/model.py:41-47,254-274`):
 `install_w4a16(model)` replaces every decoder linear with a `W4A16Linear` and, optionally, each MLP's
-gate/up pair with one fused gate_up + SwiGLU launch.
+gate/up pair with one fused gate_up + SwiGLU launch. `install_w4a16_compressed(model, state, config)` does the
+same from a compressed-tensors pack-quantized checkpoint (`from_pack_quantized` per Linear): the checkpoint's
+packed words are this format's codes already, so a published INT4 model serves with no dense copy.
 """
 
 from __future__ import annotations
@@ -174,4 +176,83 @@ def install_w4a16(model: nn.Module, group: int = 128, fuse_gate_up: bool = True)
         else:
             for name in LINEAR_NAMES[4:]:
                 setattr(layer.mlp, name, W4A16Linear.from_linear(getattr(layer.mlp, name), group))
+    return model
+
+
+# ---- compressed-tensors "pack-quantized" checkpoints straight into W4A16 buffers ------------------------------
+
+
+def from_pack_quantized(tensors: dict[str, torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, None, int]:
+    """One Linear of a compressed-tensors pack-quantized (INT4 W4A16) checkpoint -> (qweight, scales, None, group).
+
+    `tensors` holds the module's `weight_packed` int32 [out, in/8], `weight_scale` [out, in/group] and
+    `weight_shape` (keys without the module prefix), as `src/fastserve/quant/compressed.py:56-69` reads them. The
+    checkpoint's grid is symmetric and each nibble stores q + 8 (`pack_int`, `compressed.py:25-41`): that is this
+    module's unsigned code layout with the implicit zero point 8 (`qzeros=None`), so the packed words are used
+    as they are and no dense weight is ever built. The scales become fp16; a bf16 scale with magnitude in fp16's
+    normal range [2^-14, 65504] converts exactly, and any scale that would change raises ValueError (the
+    weights the kernel multiplies are then exactly those `dequantize_linear` builds, before its bf16 rounding).
+    """
+    if "weight_zero_point" in tensors:
+        raise NotImplementedError("asymmetric pack-quantized checkpoints are not read (nor by compressed.py:58-59)")
+    if "weight_packed" not in tensors:
+        raise ValueError("not a pack-quantized Linear: no weight_packed")
+    packed, scale = tensors["weight_packed"], tensors["weight_scale"]
+    out, cols = (int(v) for v in tensors["weight_shape"])
+    if packed.dtype != torch.int32 or packed.dim() != 2 or packed.shape[0] != out or packed.shape[1] * 8 < cols:
+        raise ValueError(f"weight_packed must be int32 [{out}, {(cols + 7) // 8}], got {tuple(packed.shape)}")
+    if cols % 8 != 0 or packed.shape[1] * 8 != cols:
+        raise ValueError(f"input features {cols} must fill whole int32 words (a multiple of 8)")
+    if scale.dim() != 2 or scale.shape[0] != out or cols % scale.shape[1] != 0:
+        raise ValueError(f"weight_scale must be [{out}, groups] with groups dividing {cols}")
+    group = cols // scale.shape[1]
+    scales = scale.to(torch.float16)
+    if not torch.equal(scales.to(scale.dtype), scale) or not torch.isfinite(scales).all():
+        raise ValueError("weight_scale does not convert exactly to fp16 (a scale outside fp16's normal range)")
+    return packed.contiguous(), scales.contiguous(), None, group
+
+
+def _pack_quantized_parts(state: dict[str, torch.Tensor], module: str) -> dict[str, torch.Tensor]:
+    parts = {n: state[f"{module}.{n}"] for n in ("weight_packed", "weight_scale", "weight_shape", "weight_zero_point")
+             if f"{module}.{n}" in state}
+    if "weight_packed" not in parts:
+        raise ValueError(f"{module}: no weight_packed in the checkpoint")
+    return parts
+
+
+@torch.no_grad()
+def install_w4a16_compressed(model: nn.Module, state: dict[str, torch.Tensor], quantization_config: dict,
+                             fuse_gate_up: bool = True, prefix: str = "model.layers") -> nn.Module:
+    """`install_w4a16` fed from a pack-quantized checkpoint's state dict instead of dense weights: every decoder
+    linear of the model becomes a W4A16Linear over the checkpoint's own codes and scales (and each gate/up pair
+    one fused launch, their rows interleaved), so a published INT4 checkpoint serves without the dense BF16 copy
+    that `compressed.dense_state_dict` (`compressed.py:72-97`) builds. Buffers land on each module's device."""
+    if quantization_config.get("format") != "pack-quantized":
+        raise ValueError(f"expected a pack-quantized checkpoint, got format {quantization_config.get('format')!r}")
+    bits = {g["weights"]["num_bits"] for g in quantization_config["config_groups"].values()}
+    if bits != {4}:
+        raise NotImplementedError(f"4-bit weights expected, got {sorted(bits)}")
+    for i, layer in enumerate(model.model.layers):
+        def load(sub: str, name: str, like: nn.Module):
+            qw, sc, _, group = from_pack_quantized(_pack_quantized_parts(state, f"{prefix}.{i}.{sub}.{name}"))
+            device = next(like.parameters()).device
+            return qw.to(device), sc.to(device), group
+
+        attn = layer.self_attn
+        for name in LINEAR_NAMES[:4]:
+            qw, sc, group = load("self_attn", name, getattr(attn, name))
+            setattr(attn, name, W4A16Linear(qw, sc, None, group))
+        mlp = layer.mlp
+        if fuse_gate_up:
+            gq, gs, group = load("mlp", "gate_proj", mlp.gate_proj)
+            uq, us, group_up = load("mlp", "up_proj", mlp.up_proj)
+            if group_up != group:
+                raise ValueError("gate_proj and up_proj must share a group size to be fused")
+            dq, ds, dgroup = load("mlp", "down_proj", mlp.down_proj)
+            layer.mlp = W4A16GateUpMLP((interleave_rows(gq, uq), interleave_rows(gs, us), None),
+                                       W4A16Linear(dq, ds, None, dgroup), group)
+        else:
+            for name in LINEAR_NAMES[4:]:
+                qw, sc, group = load("mlp", name, getattr(mlp, name))
+                setattr(mlp, name, W4A16Linear(qw, sc, None, group))
     return model

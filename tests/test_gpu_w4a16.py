@@ -215,3 +215,25 @@ def test_bad_arguments_raise_value_error():
         w4a16_linear(acts(1, 128).cuda(), qweight, scales, qzeros)  # wrong K
     with pytest.raises(ValueError):
         w4a16_linear(acts(1, 256).cuda(), qweight, scales, qzeros, group=64)  # scales do not match the group
+
+
+@pytest.mark.parametrize("m", [1, 4, 64])
+def test_pack_quantized_checkpoint_serves_without_a_dense_copy(m):
+    """A compressed-tensors INT4 Linear (q + 8 nibbles, bf16 group scales) loaded by from_pack_quantized runs the
+    kernels on the checkpoint's own words; the result matches the reference's dense path (dequantize_linear,
+    compressed.py:56-69, then nn.Linear) within the north-star tolerance."""
+    from bpt_b200.kernels.w4a16 import from_pack_quantized, w4a16_kernel, w4a16_linear
+
+    n, k = 2048, 2048
+    g = torch.Generator().manual_seed(m)
+    q = torch.randint(-8, 8, (n, k), generator=g)
+    scale = (torch.rand(n, k // 128, generator=g) * 0.004 + 1e-3).to(torch.bfloat16)
+    parts = {"weight_packed": ow4.pack_nibbles_int32((q + 8).to(torch.uint8)), "weight_scale": scale,
+             "weight_shape": torch.tensor([n, k])}
+    qweight, scales, qzeros, group = from_pack_quantized(parts)
+    x = acts(m, k, seed=m + 1)
+    got = w4a16_linear(x.cuda(), qweight.cuda(), scales.cuda(), qzeros, group=group).cpu().float()
+    dense = (q.float() * scale.float().repeat_interleave(128, dim=1)).to(torch.bfloat16)  # dequantize_linear
+    torch.testing.assert_close(got, torch.nn.functional.linear(x.float(), dense.float()), **TOL)
+    own = ow4.w4a16_linear(x, qweight, scales, None, group, dense_bf16=w4a16_kernel(m, n, k, group, False) == "tcgen05")
+    torch.testing.assert_close(got, own.float(), **TOL)
