@@ -44,7 +44,7 @@ def _rank_main(rank: int, world: int, port: int, results):
 
 def test_two_gloo_ranks_combine_like_the_gpu_run():
     world = 2
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()  # no fork of a process that already runs torch threads
     results = manager.dict()
     mp.spawn(_rank_main, args=(world, _free_port(), results), nprocs=world, join=True)
     for rank in range(world):
