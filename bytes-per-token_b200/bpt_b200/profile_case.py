@@ -7,6 +7,8 @@
     python -m bpt_b200.profile_case gate-up-m64      (gate-up-m256)
     python -m bpt_b200.profile_case norm-quant       (one [16384, 2048] bf16 rms_norm_int8 per launch)
     python -m bpt_b200.profile_case norm-quant-sweep
+    python -m bpt_b200.profile_case kivi-sweep       (contiguous KIVI decode attention, bits 4 / 8 / 16)
+    python -m bpt_b200.profile_case kv-write-sweep   (paged FP8 / INT8 cache writes, KIVI group quantize)
 
 Each kernel case builds its seeded synthetic inputs once, then launches the kernel `--launches` times back to
 back and prints the mean device time per launch (CUDA events; not a benchmark number under a profiler).
@@ -164,6 +166,126 @@ def _norm_quant_sweep() -> None:
         torch.cuda.empty_cache()
 
 
+def _graph_us(calls, copies: int, reps: int = 10) -> float:
+    """us per call of `calls()` (which makes `copies` calls), replayed as one CUDA graph after warm-up."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        calls()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        calls()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1e3 / (reps * copies)
+    del graph
+    return us
+
+
+def kivi_bytes(batch: int, kv_heads: int, tokens: int, head_dim: int, bits: int, group: int = 32) -> int:
+    """K and V codes, the keys' per-channel grids (fp16 scale + zero per group of tokens), the values' per-token
+    grids, for every token of every sequence and KV head (q and the output are negligible)."""
+    if bits == 16:
+        return batch * kv_heads * tokens * head_dim * 2 * 2
+    codes = head_dim // 2 if bits == 4 else head_dim
+    return batch * kv_heads * tokens * (2 * codes + 2 * 2 * head_dim // group + 2 * 2)
+
+
+def _kivi_sweep() -> None:
+    """The contiguous KIVI path (`attend` over a QuantKV: split kernel + merge kernel) on the reference's quoted
+    case, one 32k-token sequence with 16 Q / 8 KV heads and D 128, and on a batch of 8 such sequences."""
+    from .kernels.kv_write import quantize_kv
+
+    peak = _peak_gbs()
+    print("| batch x tokens | bits | us per call | GB/s | of HBM peak |")
+    print("|---|---|---|---|---|")
+    hq, hkv, d, t = 16, 8, 128, 32768
+    for batch in (1, 8):
+        for bits in (4, 8, 16):
+            nbytes = kivi_bytes(batch, hkv, t, d, bits)
+            copies = max(2, min(8, int(400e6 // nbytes)))
+            g = torch.Generator(device="cuda").manual_seed(batch * 100 + bits)
+            caches = []
+            for _ in range(copies):
+                k = torch.randn(batch, hkv, t, d, generator=g, device="cuda").to(torch.bfloat16)
+                v = torch.randn(batch, hkv, t, d, generator=g, device="cuda").to(torch.bfloat16)
+                caches.append(quantize_kv(k, v, bits))
+                del k, v
+            q = torch.randn(batch, hq, d, generator=g, device="cuda").to(torch.bfloat16)
+            lengths = torch.full((batch,), t, dtype=torch.int32, device="cuda")
+            out = torch.empty(batch, hq, d, device="cuda")
+
+            def calls():
+                for kv in caches:
+                    attend(q, kv, lengths, 1.0 / math.sqrt(d), out=out, tokens=t)
+
+            us = _graph_us(calls, copies)
+            gbs = nbytes / us / 1e3
+            print(f"| {batch} x {t} | {bits} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} |", flush=True)
+            del caches
+            torch.cuda.empty_cache()
+
+
+def _kv_write_sweep() -> None:
+    """The paged cache write (quantize_kv_paged: FP8 per-tensor scale, INT8 per (token, head) fp16 scale) for one
+    decode token per sequence and for 512-token blocks, and the KIVI group quantize (quantize_kv_into)."""
+    from .kernels.kv_write import empty_quant_kv, quantize_kv_into, quantize_kv_paged
+
+    peak = _peak_gbs()
+    print("| write | shape (B x Hkv x tokens x D, bf16 in) | us per call | GB/s | of HBM peak |")
+    print("|---|---|---|---|---|")
+    hkv, d, bs = 8, 128, 16
+    for kind in ("fp8", "int8"):
+        for batch, q in ((64, 1), (32, 512)):
+            elems = batch * hkv * q * d
+            nbytes = 2 * elems * 2 + 2 * elems + (2 * batch * hkv * q * 2 if kind == "int8" else 0) + 2 * batch * q * 4
+            copies = max(2, min(40, int(300e6 // nbytes)))
+            g = torch.Generator(device="cuda").manual_seed(batch + q)
+            blocks = batch * q // bs + batch
+            kvs = [workloads.empty_pool(kind, blocks, bs, hkv, d, "cuda", None) for _ in range(copies)]
+            ks = [torch.randn(batch, hkv, q, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(copies)]
+            vs = [torch.randn(batch, hkv, q, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(copies)]
+            slot = torch.arange(batch * q, device="cuda", dtype=torch.int32).view(batch, q)
+            wb, wo = (slot // bs).contiguous(), (slot % bs).contiguous()
+
+            def calls():
+                for i in range(copies):
+                    quantize_kv_paged(ks[i], vs[i], kvs[i], wb, wo)
+
+            us = _graph_us(calls, copies)
+            gbs = nbytes / us / 1e3
+            print(f"| paged {kind} | {batch} x {hkv} x {q} x {d} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} |", flush=True)
+            del kvs, ks, vs
+            torch.cuda.empty_cache()
+    for bits in (4, 8):
+        batch, t = 8, 4096
+        elems = batch * hkv * t * d
+        nbytes = 2 * elems * 2 + kivi_bytes(batch, hkv, t, d, bits)
+        copies = 2
+        g = torch.Generator(device="cuda").manual_seed(bits)
+        ks = [torch.randn(batch, hkv, t, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(copies)]
+        vs = [torch.randn(batch, hkv, t, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(copies)]
+        caches = [empty_quant_kv(batch, hkv, t, d, bits, 32, "cuda") for _ in range(copies)]
+
+        def calls():
+            for i in range(copies):
+                quantize_kv_into(ks[i], vs[i], caches[i], 0)
+
+        us = _graph_us(calls, copies)
+        gbs = nbytes / us / 1e3
+        print(f"| KIVI {bits}-bit quantize | {batch} x {hkv} x {t} x {d} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} |",
+              flush=True)
+        del ks, vs, caches
+        torch.cuda.empty_cache()
+
+
 def _gate_up(m: int, launches: int) -> float:
     """The fused gate_up linear of config 4 (12288 x 2048) at M tokens: one weight copy."""
     from .kernels.w4a16 import w4a16_gate_up_silu
@@ -198,7 +320,8 @@ def _time(fn, launches: int) -> float:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("case", choices=["attention-config2", "attention-config3", "gemv-config1", "w4a16-sweep",
-                                     "gate-up-m64", "gate-up-m256", "norm-quant", "norm-quant-sweep"])
+                                     "gate-up-m64", "gate-up-m256", "norm-quant", "norm-quant-sweep", "kivi-sweep",
+                                     "kv-write-sweep"])
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
     if args.case == "w4a16-sweep":
@@ -206,6 +329,12 @@ def main() -> None:
         return
     if args.case == "norm-quant-sweep":
         _norm_quant_sweep()
+        return
+    if args.case == "kivi-sweep":
+        _kivi_sweep()
+        return
+    if args.case == "kv-write-sweep":
+        _kv_write_sweep()
         return
     if args.case == "norm-quant":
         us = _norm_quant(args.launches)
