@@ -221,6 +221,16 @@ __device__ __forceinline__ uint16_t float2_to_e4m3x2(float lo, float hi) {
   return r;
 }
 
+// y / b, correctly rounded, from r = RN(1 / b) (computed once per divisor, e.g. with __frcp_rn): q = RN(y * r) is
+// within one ulp of y / b, and with the exact remainder e = y - q * b (one FMA), RN(q + e * r) is the correctly
+// rounded quotient (Markstein's theorem; P. Markstein, IBM J. Res. Dev. 34(1), 1990; Muller et al., Handbook of
+// Floating-Point Arithmetic, 2nd ed., 4.9), barring underflow of e, i.e. for quotients far above 2^-100.
+__device__ __forceinline__ float div_by(float y, float b, float r) {
+  const float q = __fmul_rn(y, r);
+  const float e = __fmaf_rn(-q, b, y);
+  return __fmaf_rn(e, r, q);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -79,15 +79,8 @@ __device__ __forceinline__ void store_chunk(T* p, const float (&v)[CH]) {
   }
 }
 
-// y / b, correctly rounded, from r = RN(1 / b): q = RN(y * r) is within one ulp of y / b, and with the exact
-// remainder e = y - q * b (one FMA), RN(q + e * r) is the correctly rounded quotient (Markstein's theorem; P.
-// Markstein, IBM J. Res. Dev. 34(1), 1990; Muller et al., Handbook of Floating-Point Arithmetic, 2nd ed., 4.9),
-// barring underflow of e, which here only touches quotients far below 0.5 (code 0 either way).
-__device__ __forceinline__ float div_by(float y, float b, float r) {
-  const float q = __fmul_rn(y, r);
-  const float e = __fmaf_rn(-q, b, y);
-  return __fmaf_rn(e, r, q);
-}
+// div_by (common.cuh): y / b correctly rounded from the divisor's reciprocal; its only exception, an underflowing
+// remainder, touches quotients far below 0.5 here (code 0 either way).
 
 // clamp(rint(v), -128, 127) as int8: round to nearest even and saturate in one conversion
 __device__ __forceinline__ int8_t to_code(float v) {
