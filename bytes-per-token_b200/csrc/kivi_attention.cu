@@ -82,6 +82,26 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
   const int t0 = s * a.split;
   const int t1 = min(L, t0 + a.split);
 
+  // The split's code rows and grids are requested into L2 up front (one 128-byte line per thread in turn): the
+  // group loop's chain of dependent loads (grids, key rows, value grids, value rows) then waits on L2, not DRAM.
+  if (t1 > t0) {
+    const int64_t r0 = (int64_t)bh * a.t_max + t0, nt = t1 - t0;
+    auto prefetch = [&](const void* p, int64_t bytes) {
+      const char* c = static_cast<const char*>(p);
+      for (int64_t o = int64_t(tid) * 128; o < bytes; o += int64_t(kWarps * 32) * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(c + o));
+    };
+    prefetch(a.k_codes + r0 * ROWB, nt * ROWB);
+    prefetch(a.v_codes + r0 * ROWB, nt * ROWB);
+    if constexpr (BITS != 16) {
+      prefetch(a.v_scale + r0, nt * 2);
+      prefetch(a.v_zero + r0, nt * 2);
+      const int64_t g0 = (int64_t)bh * a.n_groups + t0 / kGroup, ng = (nt + kGroup - 1) / kGroup;
+      prefetch(a.k_scale + g0 * D, ng * D * 2);
+      prefetch(a.k_zero + g0 * D, ng * D * 2);
+    }
+  }
+
   for (int i = tid; i < REP * D; i += kWarps * 32) {
     const int r = i / D, d = i % D;
     q_s[r][d] = qload(a.q, a.q_dtype, (int64_t)b * a.q_sb + (int64_t)(h * REP + r) * a.q_sh + d) * a.sm_scale * kLog2e;
