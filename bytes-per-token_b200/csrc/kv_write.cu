@@ -1,9 +1,10 @@
 // The quantized KV-cache write path.
 //
-// bpt_paged_kv_write: one warp per (K or V, sequence, KV head, new token). The warp reads the head vector,
-// quantizes it (FP8: x / scale rounded to E4M3 with saturation; INT8: an fp16 scale from the vector's absmax,
-// then codes), and stores D bytes to slot (block, offset) of the pool, plus the scale for INT8. Division is
-// IEEE (__fdiv_rn) and rounding is half-to-even, so the codes equal the CPU reference's bit for bit.
+// bpt_paged_kv_write: one warp per (K or V, sequence, KV head, new token). The warp reads the head vector (one
+// vector load per lane where strides allow), quantizes it (FP8: x / scale rounded to E4M3 with saturation; INT8:
+// an fp16 scale from the vector's absmax, then codes), and stores D bytes to slot (block, offset) of the pool (one
+// word per lane), plus the scale for INT8. Quotients are correctly rounded (div_by: the divisor's reciprocal and
+// one remainder correction) and rounding is half-to-even, so the codes equal the CPU reference's bit for bit.
 //
 // bpt_kivi_quantize: the KIVI grids of kernels/reference.py for whole key groups. Keys: one thread per
 // (sequence, head, group, channel [pair]) over the group's tokens; values: one warp per token over its
@@ -18,7 +19,21 @@ __device__ __forceinline__ float ld(const void* p, int64_t i) {
   return load_as_float<DT>(p, i);
 }
 
-template <int DT, int VPL, int KIND>
+// VPL values of type DT (VPL * sizeof(DT) bytes, aligned to that size up to 16) as floats
+template <int DT, int VPL>
+__device__ __forceinline__ void load_vec(const void* src, int64_t i, float (&x)[VPL]) {
+  constexpr int kBytes = VPL * (DT == BPT_DTYPE_F32 ? 4 : 2);
+  struct alignas(kBytes < 16 ? kBytes : 16) Chunk {
+    uint8_t b[kBytes];
+  };
+  const Chunk c = *reinterpret_cast<const Chunk*>(static_cast<const uint8_t*>(src) + i * (kBytes / VPL));
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) x[j] = load_as_float<DT>(c.b, j);
+}
+
+// VEC: a lane's VPL values load as one aligned vector and its codes store as one VPL-byte word (the host checks
+// strides and pointers); otherwise element by element.
+template <int DT, int VPL, int KIND, bool VEC>
 __global__ void paged_kv_write_kernel(const void* __restrict__ k, const void* __restrict__ v, int64_t sb, int64_t sh,
                                       int64_t sq, int B, int Hkv, int Q, const int32_t* __restrict__ wblocks,
                                       const int32_t* __restrict__ woffsets, uint8_t* __restrict__ k_pool,
@@ -33,29 +48,44 @@ __global__ void paged_kv_write_kernel(const void* __restrict__ k, const void* __
   pdl_wait();
   const bool is_v = wid >= per_tensor;
   const int64_t idx = is_v ? wid - per_tensor : wid;
-  const int q = int(idx % Q);
-  const int h = int((idx / Q) % Hkv);
-  const int b = int(idx / ((int64_t)Q * Hkv));
+  int q, h, b;
+  if (per_tensor < (int64_t(1) << 31)) {  // 32-bit index arithmetic (64-bit division is a long sequence)
+    const uint32_t i32 = uint32_t(idx), qh = uint32_t(Q) * uint32_t(Hkv);
+    b = int(i32 / qh);
+    const uint32_t rest = i32 - uint32_t(b) * qh;
+    h = int(rest / uint32_t(Q));
+    q = int(rest - uint32_t(h) * uint32_t(Q));
+  } else {
+    q = int(idx % Q);
+    h = int((idx / Q) % Hkv);
+    b = int(idx / ((int64_t)Q * Hkv));
+  }
+  const void* src = is_v ? v : k;
+  const int64_t base = (int64_t)b * sb + (int64_t)h * sh + (int64_t)q * sq + lane * VPL;
+  // lane owns dims [lane*VPL, lane*VPL + VPL): contiguous bytes in the pool row; the values are requested with
+  // the slot, before either is used
+  float x[VPL];
+  if constexpr (VEC) {
+    load_vec<DT, VPL>(src, base, x);
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) x[j] = ld<DT>(src, base + j);
+  }
   const int32_t blk = wblocks[(int64_t)b * Q + q];
   const int32_t off = woffsets[(int64_t)b * Q + q];
   if (blk < 0 || blk >= num_blocks || off < 0 || off >= block_size) {
     if (lane == 0) record_error(blk < 0 || blk >= num_blocks ? kDevErrBlockIndex : kDevErrSlotIndex);
     return;
   }
-  const void* src = is_v ? v : k;
-  const int64_t base = (int64_t)b * sb + (int64_t)h * sh + (int64_t)q * sq;
-  // lane owns dims [lane*VPL, lane*VPL + VPL): contiguous bytes in the pool row
-  float x[VPL];
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) x[j] = ld<DT>(src, base + lane * VPL + j);
   const int64_t slot = ((int64_t)blk * block_size + off) * Hkv + h;
   uint8_t* dst = (is_v ? v_pool : k_pool) + slot * D + lane * VPL;
-  uint8_t bytes[VPL];
+  alignas(8) uint8_t bytes[VPL];
   if constexpr (KIND == BPT_KV_FP8) {
     const float s = is_v ? v_scale : k_scale;
+    const float rs = __frcp_rn(s);
 #pragma unroll
     for (int j = 0; j < VPL; j += 2) {
-      const uint16_t two = float2_to_e4m3x2(__fdiv_rn(x[j], s), __fdiv_rn(x[j + 1], s));
+      const uint16_t two = float2_to_e4m3x2(div_by(x[j], s, rs), div_by(x[j + 1], s, rs));
       bytes[j] = uint8_t(two & 0xFF);
       bytes[j + 1] = uint8_t(two >> 8);
     }
@@ -67,15 +97,24 @@ __global__ void paged_kv_write_kernel(const void* __restrict__ k, const void* __
     __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
     if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
     const float s = __half2float(s16);
+    const float rs = __frcp_rn(s);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
-      const float c = fminf(fmaxf(rintf(__fdiv_rn(x[j], s)), -128.f), 127.f);
+      const float c = fminf(fmaxf(rintf(div_by(x[j], s, rs)), -128.f), 127.f);
       bytes[j] = uint8_t(int8_t(int(c)));
     }
     if (lane == 0) (is_v ? v_scales : k_scales)[slot] = s16;
   }
+  if constexpr (VEC && VPL == 8) {
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(bytes);
+  } else if constexpr (VEC && VPL == 4) {
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(bytes);
+  } else if constexpr (VEC && VPL == 2) {
+    *reinterpret_cast<uint16_t*>(dst) = *reinterpret_cast<const uint16_t*>(bytes);
+  } else {
 #pragma unroll
-  for (int j = 0; j < VPL; ++j) dst[j] = bytes[j];
+    for (int j = 0; j < VPL; ++j) dst[j] = bytes[j];
+  }
 }
 
 template <int DT>
@@ -86,10 +125,21 @@ int paged_write_dt(const void* k, const void* v, int64_t sb, int64_t sh, int64_t
   const int threads = 256;
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
   BPT_REQUIRE(blocks < (1ll << 31), BPT_ERR_INVALID, "paged kv write: too many tokens");
+  // vector accesses: every row start (and each lane's VPL values) aligned to the vector, pools to the code word
+  const int64_t vpl = D / 32, esz = DT == BPT_DTYPE_F32 ? 4 : 2;
+  const int64_t vbytes = std::min<int64_t>(vpl * esz, 16);
+  auto al = [](const void* p, int64_t n) { return (reinterpret_cast<uintptr_t>(p) % uintptr_t(n)) == 0; };
+  const bool vec = sb % vpl == 0 && sh % vpl == 0 && sq % vpl == 0 && al(k, vbytes) && al(v, vbytes) &&
+                   al(kp, vpl) && al(vp, vpl);
 #define BPT_KVW(VPL, KIND)                                                                                        \
-  paged_kv_write_kernel<DT, VPL, KIND><<<unsigned(blocks), threads, 0, stream>>>(                                 \
-      k, v, sb, sh, sq, int(B), int(Hkv), int(Q), wb, wo, static_cast<uint8_t*>(kp), static_cast<uint8_t*>(vp), ks, \
-      vs, static_cast<__half*>(kss), static_cast<__half*>(vss), int(bs), nb)
+  if (vec)                                                                                                        \
+    paged_kv_write_kernel<DT, VPL, KIND, true><<<unsigned(blocks), threads, 0, stream>>>(                         \
+        k, v, sb, sh, sq, int(B), int(Hkv), int(Q), wb, wo, static_cast<uint8_t*>(kp), static_cast<uint8_t*>(vp),   \
+        ks, vs, static_cast<__half*>(kss), static_cast<__half*>(vss), int(bs), nb);                               \
+  else                                                                                                            \
+    paged_kv_write_kernel<DT, VPL, KIND, false><<<unsigned(blocks), threads, 0, stream>>>(                        \
+        k, v, sb, sh, sq, int(B), int(Hkv), int(Q), wb, wo, static_cast<uint8_t*>(kp), static_cast<uint8_t*>(vp),   \
+        ks, vs, static_cast<__half*>(kss), static_cast<__half*>(vss), int(bs), nb)
   if (kind == BPT_KV_FP8) {
     if (D == 64) BPT_KVW(2, BPT_KV_FP8);
     else if (D == 128) BPT_KVW(4, BPT_KV_FP8);
