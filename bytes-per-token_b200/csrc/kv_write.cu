@@ -164,10 +164,20 @@ __global__ void kivi_keys_kernel(const void* __restrict__ k, int B, int Hkv, int
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)B * Hkv * (T / group) * per_group;
   if (tid >= total) return;
-  const int c = int(tid % per_group);
-  const int gi = int((tid / per_group) % (T / group));
-  const int h = int((tid / ((int64_t)per_group * (T / group))) % Hkv);
-  const int b = int(tid / ((int64_t)per_group * (T / group) * Hkv));
+  int c, gi, h, b;
+  if (total < (int64_t(1) << 31)) {  // 32-bit index arithmetic (64-bit division is a long sequence)
+    const uint32_t i = uint32_t(tid), pg = uint32_t(per_group), ng = uint32_t(T / group);
+    const uint32_t r1 = i / pg, r2 = r1 / ng;
+    c = int(i - r1 * pg);
+    gi = int(r1 - r2 * ng);
+    b = int(r2 / uint32_t(Hkv));
+    h = int(r2 - uint32_t(b) * uint32_t(Hkv));
+  } else {
+    c = int(tid % per_group);
+    gi = int((tid / per_group) % (T / group));
+    h = int((tid / ((int64_t)per_group * (T / group))) % Hkv);
+    b = int(tid / ((int64_t)per_group * (T / group) * Hkv));
+  }
   const float qmax = float((1 << bits) - 1);
   const int nch = bits == 4 ? 2 : 1;
   uint8_t out_codes[2][64];  // at most group 64 tokens per thread
@@ -183,13 +193,14 @@ __global__ void kivi_keys_kernel(const void* __restrict__ k, int B, int Hkv, int
     __half s16 = __float2half_rn(__fdiv_rn(hi - lo, qmax));
     if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
     const float s = __half2float(s16);
-    const float z = fminf(fmaxf(rintf(__fdiv_rn(-lo, s)), 0.f), qmax);
+    const float rs = __frcp_rn(s);
+    const float z = fminf(fmaxf(rintf(div_by(-lo, s, rs)), 0.f), qmax);
     const int64_t g_out = ((int64_t)b * Hkv + h) * n_groups + (t0 / group) + gi;
     kscale[g_out * D + d] = s16;
     kzero[g_out * D + d] = __float2half_rn(z);
     for (int t = 0; t < group; ++t) {
       const float x = load_as_float<DT>(k, src0 + (int64_t)t * D);
-      out_codes[ch][t] = uint8_t(fminf(fmaxf(rintf(__fdiv_rn(x, s)) + z, 0.f), qmax));
+      out_codes[ch][t] = uint8_t(fminf(fmaxf(rintf(div_by(x, s, rs)) + z, 0.f), qmax));
     }
   }
   const int row_bytes = bits == 4 ? D / 2 : D;
@@ -210,8 +221,16 @@ __global__ void kivi_values_kernel(const void* __restrict__ v, int B, int Hkv, i
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int64_t total = (int64_t)B * Hkv * T;
   if (wid >= total) return;  // whole warps exit together (blockDim a multiple of 32)
-  const int t = int(wid % T);
-  const int64_t bh = wid / T;
+  int t;
+  int64_t bh;
+  if (total < (int64_t(1) << 31)) {  // 32-bit index arithmetic
+    const uint32_t w = uint32_t(wid), q = w / uint32_t(T);
+    bh = q;
+    t = int(w - q * uint32_t(T));
+  } else {
+    t = int(wid % T);
+    bh = wid / T;
+  }
   const int64_t src0 = (bh * T + t) * D;
   float lo = 0.f, hi = 0.f;
   for (int d = lane; d < D; d += 32) {
@@ -228,10 +247,11 @@ __global__ void kivi_values_kernel(const void* __restrict__ v, int B, int Hkv, i
   __half s16 = __float2half_rn(__fdiv_rn(hi - lo, qmax));
   if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
   const float s = __half2float(s16);
-  const float z = fminf(fmaxf(rintf(__fdiv_rn(-lo, s)), 0.f), qmax);
+  const float rs = __frcp_rn(s);
+  const float z = fminf(fmaxf(rintf(div_by(-lo, s, rs)), 0.f), qmax);
   for (int d = lane; d < D; d += 32) {
     const float x = load_as_float<DT>(v, src0 + d);
-    stage[wl][d] = uint8_t(fminf(fmaxf(rintf(__fdiv_rn(x, s)) + z, 0.f), qmax));
+    stage[wl][d] = uint8_t(fminf(fmaxf(rintf(div_by(x, s, rs)) + z, 0.f), qmax));
   }
   __syncwarp();
   const int64_t tok = t0 + t;
