@@ -6,7 +6,8 @@
 
 Prints one JSON line (rank 0). `value` is whole-job achieved HBM bandwidth: the algorithmic bytes of every
 rank's steps over the slowest rank's device time. `e2e` is the same metric through the public Python API with
-this step's inputs copied from pinned host memory and the results copied back inside the timed region.
+this step's inputs copied from pinned host memory and the results copied back inside the timed region (one
+staging copy each way: the kernels read and write views of one device buffer per direction).
 `--impl reference` times the reference's CPU path (the oracle port: dequantize-then-matmul and gather,
 dequantize, attend) on the host cores, on a bounded sample of the same workload.
 
@@ -20,6 +21,7 @@ their own pools (about 450 MB of KV touched per cycle), so no step finds its dat
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import math
 import os
@@ -273,30 +275,46 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     del nq_x, nq_out
     my_bytes = sum(gemv_bytes + attn_bytes[k % ATTN_BATCHES] for k in range(args.steps))
 
-    # end to end: the public API with host buffers, the step's inputs H2D and results D2H inside the region
-    pin = {
-        "x": torch.empty(1, 2048, dtype=torch.bfloat16).pin_memory(),
-        "q": [c.q.cpu().pin_memory() for c in attn],
-        "lengths": [c.lengths.cpu().pin_memory() for c in attn],
-        "table": [c.kv.block_table.cpu().pin_memory() for c in attn],
-        "y": torch.empty(1, 6144, dtype=torch.bfloat16).pin_memory(),
-        "out": torch.empty(32, 16, 128, dtype=torch.bfloat16).pin_memory(),
-    }
-    pin["x"].copy_(x.cpu())
-    h2d = pin["x"].numel() * 2 + pin["q"][0].numel() * 2 + pin["lengths"][0].numel() * 4 + pin["table"][0].numel() * 4
-    d2h = pin["y"].numel() * 2 + pin["out"].numel() * 2
+    # end to end: the public API with host buffers, the step's inputs H2D and results D2H inside the region. As a
+    # serving loop stages them, a step's inputs (x, q, lengths, block table) sit in one pinned buffer and cross in
+    # one copy into one device buffer that the kernels read through views; the two results (y, out) are views of
+    # one device buffer and come back in one copy.
+    def layout(parts):  # [(name, bytes)] -> ({name: offset}, total), each part 256-byte aligned
+        offs, at = {}, 0
+        for name, nb in parts:
+            offs[name] = at
+            at += (nb + 255) // 256 * 256
+        return offs, at
+
+    def view(buf, off, like):
+        return buf[off: off + like.numel() * like.element_size()].view(like.dtype).view(like.shape)
+
+    stage_in, pin_in, e2e_cases = [], [], []
+    for c in attn:  # each batch its own layout (block-table widths differ)
+        ioff, in_total = layout([("x", x.numel() * 2), ("q", c.q.numel() * 2), ("lengths", c.lengths.numel() * 4),
+                                 ("table", c.kv.block_table.numel() * 4)])
+        dev = torch.empty(in_total, dtype=torch.uint8, device=device)
+        xv, qv, lv, tv = (view(dev, ioff["x"], x), view(dev, ioff["q"], c.q), view(dev, ioff["lengths"], c.lengths),
+                          view(dev, ioff["table"], c.kv.block_table))
+        xv.copy_(x), qv.copy_(c.q), lv.copy_(c.lengths), tv.copy_(c.kv.block_table)
+        stage_in.append(dev)
+        pin_in.append(dev.cpu().pin_memory())
+        e2e_cases.append((xv, qv, lv, dataclasses.replace(c.kv, block_table=tv)))
+    ooff, out_total = layout([("y", y.numel() * 2), ("out", out.numel() * 2)])
+    stage_out = torch.empty(out_total, dtype=torch.uint8, device=device)
+    y_v, out_v = view(stage_out, ooff["y"], y), view(stage_out, ooff["out"], out)
+    pin_out = torch.empty(out_total, dtype=torch.uint8).pin_memory()
+    # the bytes that cross per step (padding included), averaged over the rotating batches
+    h2d, d2h = round(sum(t.numel() for t in stage_in) / len(stage_in)), out_total
 
     def e2e_step(i: int):
-        case = attn[i % ATTN_BATCHES]
+        j = i % ATTN_BATCHES
+        xv, qv, lv, kv = e2e_cases[j]
         qw, sc, qz = weights[i % GEMV_COPIES]
-        x.copy_(pin["x"], non_blocking=True)
-        case.q.copy_(pin["q"][i % ATTN_BATCHES], non_blocking=True)
-        case.lengths.copy_(pin["lengths"][i % ATTN_BATCHES], non_blocking=True)
-        case.kv.block_table.copy_(pin["table"][i % ATTN_BATCHES], non_blocking=True)
-        w4a16_linear(x, qw, sc, qz, out=y, pdl=True)
-        attend(case.q, case.kv, case.lengths, scale, out=out, tokens=4096, split=split, pdl=True, kv_ready=True)
-        pin["y"].copy_(y, non_blocking=True)
-        pin["out"].copy_(out, non_blocking=True)
+        stage_in[j].copy_(pin_in[j], non_blocking=True)
+        w4a16_linear(xv, qw, sc, qz, out=y_v, pdl=True)
+        attend(qv, kv, lv, scale, out=out_v, tokens=4096, split=split, pdl=True, kv_ready=True)
+        pin_out.copy_(stage_out, non_blocking=True)
 
     for i in range(3):
         e2e_step(i)
@@ -318,7 +336,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "nq_ms": nq_ms,
         "clocks": sampler.summary(),
     }
-    del weights, attn, pin
+    del weights, attn, stage_in, pin_in, e2e_cases, stage_out, pin_out
     torch.cuda.empty_cache()
     if not args.no_decode:
         local.update(decode_step_timing(args, rank, device, barrier))
