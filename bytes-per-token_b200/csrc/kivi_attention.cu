@@ -129,6 +129,7 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
       float bias[REP];
 #pragma unroll
       for (int r = 0; r < REP; ++r) bias[r] = 0.f;
+#pragma unroll
       for (int d = lane; d < D; d += 32) {
         const float ks = __half2float(a.k_scale[grid + d]);
         const float kz = __half2float(a.k_zero[grid + d]);
@@ -152,8 +153,15 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
     }
     __syncwarp();
 
-    // ---- QK: lane t owns token gs + t ----
+    // ---- QK: lane t owns token gs + t (its value grid requested first, so that load overlaps the dot) ----
     const int t = lane;
+    float vsc = 1.f, vz = 0.f;
+    if constexpr (BITS != 16) {
+      if (t < valid) {
+        vsc = __half2float(a.v_scale[row0 + gs + t]);
+        vz = __half2float(a.v_zero[row0 + gs + t]);
+      }
+    }
     float sc[REP];
 #pragma unroll
     for (int r = 0; r < REP; ++r) sc[r] = 0.f;
@@ -190,14 +198,6 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
         }
       }
     }
-    float vsc = 1.f, vz = 0.f;
-    if constexpr (BITS != 16) {
-      if (t < valid) {
-        vsc = __half2float(a.v_scale[row0 + gs + t]);
-        vz = __half2float(a.v_zero[row0 + gs + t]);
-      }
-    }
-
     // ---- online softmax over the group (base 2): lanes are tokens ----
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
