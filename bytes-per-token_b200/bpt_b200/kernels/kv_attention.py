@@ -205,14 +205,23 @@ def decode_attention(
     return out, lse
 
 
-def merge_partials(outs: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """[B, Hq, S, D], [B, Hq, S] -> [B, Hq, D]: the exact merge of split partials (reference.py:205-211)."""
-    device = require_cuda(outs, lses)
+def merge_partials(outs: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype = torch.float32, *,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """[B, Hq, S, D], [B, Hq, S] -> [B, Hq, D]: the exact merge of split partials (reference.py:205-211).
+
+    `out` (contiguous [B, Hq, D], float32 / float16 / bfloat16) receives the result in its own dtype instead of a
+    new tensor of `out_dtype`."""
+    device = require_cuda(outs, lses, out)
     if outs.dtype != torch.float32 or lses.dtype != torch.float32:
         raise ValueError("partials must be float32")
     outs, lses = outs.contiguous(), lses.contiguous()
     b, hq, s, d = outs.shape
-    merged = torch.empty((b, hq, d), dtype=out_dtype, device=device)
+    if out is not None:
+        if tuple(out.shape) != (b, hq, d) or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous [{b}, {hq}, {d}] tensor")
+        merged, out_dtype = out, out.dtype
+    else:
+        merged = torch.empty((b, hq, d), dtype=out_dtype, device=device)
     st = lib().bpt_merge_partials(ptr(outs), ptr(lses), b, hq, s, d, ptr(merged), dtype_code(out_dtype), stream_of(device))
     check(st, "merge_partials")
     return merged
@@ -254,12 +263,8 @@ def attend(
     launch; `kv_ready=True` adds the promise that the lengths, block table and pools are not written by the
     kernel this call follows, so the persistent kernel starts copying pages before it waits on that kernel.
     """
-    if not isinstance(kv, PagedQuantKV):
-        merged = merge_partials(*decode_attention(q, kv, lengths, scale, **launch))
-        if out is not None:
-            out.copy_(merged)
-            return out
-        return merged
+    if not isinstance(kv, PagedQuantKV):  # the merge writes straight into `out` when one is given
+        return merge_partials(*decode_attention(q, kv, lengths, scale, **launch), out=out)
     device = require_cuda(q, lengths, kv.k_pool)
     q = _q_view(q)
     lengths = _lengths(lengths)

@@ -154,6 +154,14 @@ def test_merge_partials_kernel_matches_oracle():
     want = oatt.merge_partials(outs, lses)
     torch.testing.assert_close(got.cpu(), want, rtol=1e-5, atol=1e-6)
     assert got[2].abs().sum() == 0
+    into = torch.full((3, 4, 64), float("nan"), dtype=torch.bfloat16, device="cuda")
+    assert merge_partials(outs.cuda(), lses.cuda(), out=into).data_ptr() == into.data_ptr()
+    torch.testing.assert_close(into.cpu().float(), want, rtol=1e-2, atol=1e-2)  # written in out's own dtype
+    # many splits per row (a CTA per row spreads them over its threads)
+    outs = torch.randn(2, 16, 300, 128, generator=g)
+    lses = torch.randn(2, 16, 300, generator=g) * 4
+    torch.testing.assert_close(merge_partials(outs.cuda(), lses.cuda()).cpu(), oatt.merge_partials(outs, lses),
+                               rtol=1e-5, atol=1e-6)
 
 
 def test_out_of_range_block_entry_is_recorded_not_read():
