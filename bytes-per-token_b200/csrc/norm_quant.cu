@@ -11,8 +11,9 @@
 // The row is read once: its elements stay in registers (16-byte loads when the row, the weight and the strides
 // allow it, else one element at a time) and the three passes (sum of squares, max of |y|, the codes) run on that
 // copy. Two launch shapes:
-// - 512 rows or more, each of up to 512 chunks (4,096 16-bit or 2,048 fp32 elements; 512 on the one-element
-//   path): one WARP per row, eight rows per CTA, warps persistent over rows, reductions by shuffles only. A row
+// - 512 rows or more, each of up to 1,024 chunks (8,192 16-bit or 4,096 fp32 elements; 1,024 on the one-element
+//   path; past 512 chunks one CTA per SM): one WARP per row, eight rows per CTA, warps persistent over rows,
+//   reductions by shuffles only. A row
 //   is a few KB, so an SM needs many rows in flight to cover HBM latency: the row is kept as packed 16-byte
 //   words, there is no block barrier, and the arithmetic runs two elements per instruction on the packed fp32
 //   pipe (the kernel is otherwise instruction-bound: ~20 operations per element).
@@ -288,7 +289,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, int64_t n, int lane) 
 // CH = 16 / sizeof(T) (16-byte chunks) or 1; lane l holds chunks l, l + 32, ..., NPER of them at most. Warps are
 // persistent over rows (row, row + all warps, ...); each asks L2 for its next row before working on this one.
 template <typename T, int CH, int NPER>
-__global__ void __launch_bounds__(32 * kRowsPerCta, 2) rms_norm_int8_rows_kernel(const NormQuantArgs a, int64_t rows,
+__global__ void __launch_bounds__(32 * kRowsPerCta, NPER <= 16 ? 2 : 1) rms_norm_int8_rows_kernel(const NormQuantArgs a, int64_t rows,
                                                                              int w_dtype) {
   pdl_launch_dependents();
   pdl_wait();  // x (and delta) may come from the previous kernel
@@ -440,7 +441,7 @@ int launch_rows_t(const NormQuantArgs& a, int64_t rows, int w_dtype, int flags, 
   return BPT_OK;
 }
 
-constexpr int kWarpMaxChunks = 32 * 16;  // the warp-per-row kernel's longest row, in chunks
+constexpr int kWarpMaxChunks = 32 * 32;  // the warp-per-row kernel's longest row, in chunks
 constexpr int64_t kWarpMinRows = 512;    // below this a CTA per row finishes sooner (more SMs share a call)
 
 template <typename T, int CH>
@@ -449,7 +450,10 @@ int launch_rows(const NormQuantArgs& a, int64_t rows, int w_dtype, int flags, cu
   if (per <= 2) return launch_rows_t<T, CH, 2>(a, rows, w_dtype, flags, stream);
   if (per <= 4) return launch_rows_t<T, CH, 4>(a, rows, w_dtype, flags, stream);
   if (per <= 8) return launch_rows_t<T, CH, 8>(a, rows, w_dtype, flags, stream);
-  return launch_rows_t<T, CH, 16>(a, rows, w_dtype, flags, stream);
+  if (per <= 16) return launch_rows_t<T, CH, 16>(a, rows, w_dtype, flags, stream);
+  // longer rows: one CTA of eight warps per SM, whose registers hold 24 or 32 chunks a lane
+  if (per <= 24) return launch_rows_t<T, CH, 24>(a, rows, w_dtype, flags, stream);
+  return launch_rows_t<T, CH, 32>(a, rows, w_dtype, flags, stream);
 }
 
 // ---- one CTA per row ----------------------------------------------------------------------------------------

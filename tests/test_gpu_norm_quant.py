@@ -128,6 +128,9 @@ def test_rms_norm_int8_rejects_bad_buffers():
     (1024, 4096, torch.float16, False),    # 16 chunks a lane, 16-bit
     (20000, 256, torch.float16, False),    # more rows than resident warps: each warp loops
     (2048, 2048, torch.bfloat16, True),    # the residual add on the warp-per-row shape
+    (600, 6144, torch.bfloat16, False),    # 24 chunks a lane: one CTA per SM
+    (512, 8192, torch.float16, True),      # 32 chunks a lane, with the residual
+    (700, 3000, torch.float32, False),     # fp32, 24 chunks of 4 a lane
 ])
 def test_rms_norm_int8_warp_per_row_shapes(rows, d, dtype, residual):
     """From 512 rows on, a warp takes a row (persistent warps, eight rows a CTA)."""
