@@ -102,6 +102,17 @@ def default_split(batch: int, kv_heads: int, tokens: int, group: int = 32, max_p
     return max(group, 1 << (per_program.bit_length() - 1))
 
 
+def kivi_attend_split(batch: int, kv_heads: int, tokens: int, group: int = 32) -> int:
+    """Tokens per program when only the merged result is wanted (`attend` over a KIVI cache): the longest power of
+    two up to 512 that still leaves 512 programs, and at least 4 key groups. Longer splits than the reference's
+    rule (`default_split`, kept by `decode_attention`, whose per-split outputs depend on it) mean fewer partials to
+    write and merge: 8 x 32k INT4 measured 234 -> 194 us at 512 tokens against 128."""
+    split = 512
+    while split > 4 * group and batch * kv_heads * -(-tokens // split) < 512:
+        split //= 2
+    return max(split, 4 * group)
+
+
 def paged_split(batch: int, tokens: int, block_size: int = 16, sms: int = 148) -> int:
     """Tokens per CTA for the paged kernel, whose CTA covers every KV head of one sequence's split.
 
@@ -264,6 +275,9 @@ def attend(
     kernel this call follows, so the persistent kernel starts copying pages before it waits on that kernel.
     """
     if not isinstance(kv, PagedQuantKV):  # the merge writes straight into `out` when one is given
+        if launch.get("split") is None:
+            launch = dict(launch, split=kivi_attend_split(q.shape[0], kv.k_codes.shape[1],
+                                                           launch.get("tokens") or kv.k_codes.shape[2], kv.group))
         return merge_partials(*decode_attention(q, kv, lengths, scale, **launch), out=out)
     device = require_cuda(q, lengths, kv.k_pool)
     q = _q_view(q)
