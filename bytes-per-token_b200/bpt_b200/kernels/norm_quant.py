@@ -6,11 +6,12 @@ buffers for allocation-free, graph-captured calls. What it computes is `kernels/
 
     y = x / sqrt(mean(x²) + eps) · weight      scale = max(max|y| / 127, 1e-12)      codes = rint(y / scale)
 
-One CTA per row reads the row once into registers and runs the three passes there. Differences from the
-reference's wrapper, none visible in results:
+Each row is read once into registers and the three passes run there: from 512 rows of up to 8,192 16-bit values, a
+warp per row (eight rows per CTA, persistent CTAs); otherwise a CTA per row. Differences from the reference's
+wrapper, none visible in results:
 - a view whose rows have unit inner stride (e.g. `x[:, :64]`) is read in place through its row stride; the
   reference copies any non-contiguous input first;
-- `num_warps` is accepted for the signature and not used: the block size follows d (up to 256 threads);
+- `num_warps` is accepted for the signature and not used: the launch shape follows rows and d;
 - `delta=` adds the decoder layer's residual first (`engine/model.py:109-111`, vLLM's fused add + RMSNorm):
   x + delta, rounded to x's dtype, is normalized, and the sum goes to `x_out` when given.
 """

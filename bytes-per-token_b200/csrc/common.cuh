@@ -48,6 +48,11 @@ enum DeviceError : int {
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
+// Limits of the bounded waits: ~200 ms in normal operation (far beyond any healthy wait), ~2 ms under
+// BPT_FLAG_TEST_STALL, where a test makes a wait run out on purpose.
+constexpr uint64_t kWaitNs = 200000000ull;
+constexpr uint64_t kTestWaitNs = 2000000ull;
+
 // ---- PDL ---------------------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -57,7 +57,7 @@ struct PagedArgs {
   int out_dtype;
   float* ws_out;           // [B][n_splits][Hq][D]
   float* ws_lse;           // [B][n_splits][Hq]
-  unsigned int* ws_count;  // [B]
+  unsigned int* ws_count;  // tickets: [B] (split kernels) or [B][Hkv] (persistent kernel)
   // layout
   int page_bytes;   // kBS * Hkv * D
   int scale_bytes;  // kBS * Hkv * 2 (INT8) or 0
@@ -66,6 +66,8 @@ struct PagedArgs {
   int early;          // BPT_FLAG_KV_READY under PDL: map the pages and copy them before waiting on the predecessor
   int persist_ctas;   // CTAs (one per SM)
   int max_cta_pages;  // capacity of a CTA's page list
+  int stall;          // BPT_FLAG_TEST_STALL: CTA 0's producer stops before one page (bounded-wait tests)
+  uint64_t wait_ns;   // limit of every wait on a page's arrival
 };
 
 __device__ __forceinline__ float q_load(const void* q, int dt, int64_t i) {
@@ -506,22 +508,15 @@ int paged_common(PagedArgs& a, const void* q, int q_dtype, int64_t q_sb, int64_t
   a.ws_count = nullptr;
   a.persist_ctas = 0;
   a.max_cta_pages = 0;
+  a.stall = 0;
+  a.wait_ns = kWaitNs;
   return BPT_OK;
 }
 
 // The tensor-core kernel serves head dims 64 and 128 with up to 8 KV heads; the scalar kernel the rest.
-// BPT_PAGED_SCALAR=1 in the environment selects the scalar kernel everywhere (for comparisons).
-bool use_scalar_kernel() {
-  static const int forced = [] {
-    const char* v = getenv("BPT_PAGED_SCALAR");
-    return (v && v[0] == '1') ? 1 : 0;
-  }();
-  return forced != 0;
-}
-
 int paged_dispatch(const PagedArgs& a, int kind, int64_t D, int flags, cudaStream_t stream) {
   const int rep = a.Hq / a.Hkv;
-  if (!use_scalar_kernel() && (D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv) {
+  if ((D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv) {
     if (kind == BPT_KV_FP8)
       return D == 64 ? launch_mma_rep<64, BPT_KV_FP8>(a, rep, flags, stream)
                      : launch_mma_rep<128, BPT_KV_FP8>(a, rep, flags, stream);
@@ -551,8 +546,7 @@ int64_t split_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits
 bool persistent_applies(const PagedArgs& a, int64_t D, int64_t& cap) {
   const int G = num_sms();
   cap = (int64_t(a.B) * a.bt_stride + G - 1) / G;
-  static const int enabled = env_int("BPT_PAGED_PERSIST", 1);
-  return enabled && !use_scalar_kernel() && (D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv &&
+  return (D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv &&
          a.B <= kPersistMaxSeqs && cap <= kPersistMaxCtaPages && a.q_sh == D && a.q_sb == a.Hq * D &&
          aligned16(a.q);
 }
@@ -650,6 +644,8 @@ extern "C" int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, 
 // caller buffer. The array's name is a host-side stand-in in host code, so its device address is looked up
 // once per device (cudaGetSymbolAddress, with that device current) and passed to the kernel like any workspace.
 
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 namespace bpt {
@@ -660,23 +656,49 @@ static_assert(kNoAllocBytes > kCounterBytes, "the scratch must hold the ticket c
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
+// The array's device address per device, with the context it was looked up in: a new context (after a
+// cudaDeviceReset, or a primary context that was released and retained again) loads the module anew and may
+// place the array elsewhere, so the address is looked up again whenever the current context changes.
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mutex;
 void* g_noalloc_addr[kMaxDevices] = {};
+void* g_noalloc_ctx[kMaxDevices] = {};
 
-int noalloc_scratch(void** addr) {
+PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+  static PFN_cuCtxGetCurrent_v4000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  }();
+  return fn;
+}
+
+int noalloc_scratch(const void* q, void** addr) {
   int dev = -1;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return set_error(BPT_ERR_CUDA, "paged attend (no alloc): no current device: %s", cudaGetErrorString(err));
   BPT_REQUIRE(dev >= 0 && dev < kMaxDevices, BPT_ERR_UNSUPPORTED, "paged attend (no alloc): device %d", dev);
+  // The library picks the scratch of the current device: the caller's tensors must live there too.
+  cudaPointerAttributes attr;
+  err = cudaPointerGetAttributes(&attr, q);
+  BPT_REQUIRE(err == cudaSuccess && attr.type == cudaMemoryTypeDevice && attr.device == dev, BPT_ERR_INVALID,
+              "paged attend (no alloc): q is not device memory of the current device %d", dev);
+  PFN_cuCtxGetCurrent_v4000 get_ctx = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return set_error(BPT_ERR_CUDA, "paged attend (no alloc): no current context on device %d", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (g_noalloc_addr[dev] == nullptr || g_noalloc_ctx[dev] != static_cast<void*>(ctx)) {
     void* p = nullptr;
     err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (err != cudaSuccess || p == nullptr)
       return set_error(BPT_ERR_CUDA, "paged attend (no alloc): cannot find the scratch array on device %d: %s", dev,
                        cudaGetErrorString(err));
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = static_cast<void*>(ctx);
   }
   *addr = g_noalloc_addr[dev];
   return BPT_OK;
@@ -708,7 +730,7 @@ extern "C" int bpt_paged_attend_noalloc(const void* q, int q_dtype, int64_t q_st
               "fixed %lld (use larger splits, or bpt_paged_attend with a caller workspace)",
               (long long)B, (long long)n_splits, (long long)Hq, (long long)D, (long long)need, (long long)kNoAllocBytes);
   void* scratch = nullptr;
-  st = noalloc_scratch(&scratch);
+  st = noalloc_scratch(q, &scratch);
   if (st) return st;
   auto s = static_cast<cudaStream_t>(stream);
   // The array keeps whatever the last call left: the tickets this call uses (one per sequence, or per sequence

@@ -432,20 +432,17 @@ __global__ void __launch_bounds__(32 * kMmaMaxHkv, 1) paged_attn_mma_kernel(cons
   if (tid == 0) a.ws_count[b] = 0u;
 }
 
-// Copy layout of the pages (bit 0: keys row by row, bit 1: values row by row) and pipeline depth. The
-// environment variables BPT_PAGED_COPY / BPT_PAGED_STAGES override the defaults, for measurements.
-int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return (v && v[0]) ? atoi(v) : dflt;
-}
+// Pages are copied token row by token row to a padded pitch (COPY bit 0: keys, bit 1: values), four stages deep
+// where they fit.
+constexpr int kMmaCopy = 3;
+constexpr int kMmaStages = 4;
 
 template <int D, int REP, int KIND, int COPY>
 int launch_mma_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   PagedArgs a = a0;
   const int rowb = a.Hkv * D;
   const int stage_bytes = kBS * (rowb + ((COPY & 1) ? 16 : 0)) + kBS * (rowb + ((COPY & 2) ? 16 : 0)) + 2 * a.scale_bytes;
-  static const int stages_env = env_int("BPT_PAGED_STAGES", 4);
-  a.nst = max(2, min(stages_env, (200 * 1024) / stage_bytes));
+  a.nst = max(2, min(kMmaStages, (200 * 1024) / stage_bytes));
   auto kernel = paged_attn_mma_kernel<D, REP, KIND, COPY>;
   const int max_pages = a.split / kBS + 1;
   const int smem = a.nst * stage_bytes + a.nst * 8 + a.nst * 12 + 16 + 4 * max_pages;
@@ -466,23 +463,13 @@ int launch_mma_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   return BPT_OK;
 }
 
-template <int D, int KIND, int COPY>
-int launch_mma_copy(const PagedArgs& a, int rep, int flags, cudaStream_t stream) {
-  switch (rep) {
-    case 1: return launch_mma_t<D, 1, KIND, COPY>(a, flags, stream);
-    case 2: return launch_mma_t<D, 2, KIND, COPY>(a, flags, stream);
-    case 4: return launch_mma_t<D, 4, KIND, COPY>(a, flags, stream);
-    case 8: return launch_mma_t<D, 8, KIND, COPY>(a, flags, stream);
-  }
-  return set_error(BPT_ERR_UNSUPPORTED, "paged attention: REP=%d not in {1, 2, 4, 8}", rep);
-}
-
 template <int D, int KIND>
 int launch_mma_rep(const PagedArgs& a, int rep, int flags, cudaStream_t stream) {
-  static const int copy = env_int("BPT_PAGED_COPY", 3);
-  switch (copy) {
-    case 0: return launch_mma_copy<D, KIND, 0>(a, rep, flags, stream);
-    case 2: return launch_mma_copy<D, KIND, 2>(a, rep, flags, stream);
-    default: return launch_mma_copy<D, KIND, 3>(a, rep, flags, stream);
+  switch (rep) {
+    case 1: return launch_mma_t<D, 1, KIND, kMmaCopy>(a, flags, stream);
+    case 2: return launch_mma_t<D, 2, KIND, kMmaCopy>(a, flags, stream);
+    case 4: return launch_mma_t<D, 4, KIND, kMmaCopy>(a, flags, stream);
+    case 8: return launch_mma_t<D, 8, KIND, kMmaCopy>(a, flags, stream);
   }
+  return set_error(BPT_ERR_UNSUPPORTED, "paged attention: REP=%d not in {1, 2, 4, 8}", rep);
 }

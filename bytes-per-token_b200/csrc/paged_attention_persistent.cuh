@@ -21,6 +21,7 @@
 constexpr int kPersistMaxSeqs = 4096;
 constexpr int kMaxSmemPerCta = 227 * 1024;  // sm_100 opt-in dynamic shared memory per block
 constexpr int kPersistMaxCtaPages = 4096;
+constexpr int kPersistStages = 6;
 constexpr int64_t kCounterBytesP = 65536 * 4;  // the ticket counters, at the workspace's start (as paged_attend)
 
 struct PersistLayout {
@@ -144,7 +145,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
 
   auto wait_page = [&](int k, int st, uint32_t ph) {
     if (!misc[2]) {
-      if (mbar_wait_warp(&full[st], ph))
+      if (mbar_wait_warp(&full[st], ph, a.wait_ns))
         waited = k + 1;
       else if (lane == 0)
         misc[2] = 1;
@@ -442,7 +443,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
   settle();
   if (misc[2] && warp == 0 && lane == 0) {
     const int issued = misc[1];
-    for (int k = waited; k < issued; ++k) (void)mbar_wait(&full[k % nst], (k / nst) & 1, 20000000ull);
+    for (int k = waited; k < issued; ++k) (void)mbar_wait(&full[k % nst], (k / nst) & 1, (a.wait_ns < 20000000ull ? a.wait_ns : 20000000ull));
   }
 }
 
@@ -553,10 +554,14 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
     for (int k = 0; k < n; ++k, st = (st + 1 == a.nst) ? 0 : st + 1, eph ^= (st == 0) ? 1u : 0u) {
       if (k == pre && pre > 0) q_copies_of_first_pages();
       if (misc[2]) break;
-      if (k >= a.nst && !mbar_wait_warp(&empty[st], eph)) {
+      // BPT_FLAG_TEST_STALL: CTA 0 issues nothing from its second page on (its first, if it has one page). Every
+      // page it did issue is awaited by the consumers before they reach the missing one, so no copy is in flight.
+      if (a.stall && cta == 0 && k == min(1, n - 1)) break;
+      if (k >= a.nst && !mbar_wait_warp(&empty[st], eph, a.wait_ns)) {
         misc[2] = 1;
         break;
       }
+      if (misc[2]) break;  // a consumer gave up while this warp waited for the stage
       uint8_t* base = stages + st * lay.stage_bytes;
       const int b = pseq[k];
       const int blk = pblk[k];
@@ -624,7 +629,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
   // all consumer warps meet the same named barriers; the data they read then is stale but in bounds.
   auto wait_page = [&](int k) {
     if (!misc[2]) {
-      if (mbar_wait_warp(&full[k % a.nst], (k / a.nst) & 1))
+      if (mbar_wait_warp(&full[k % a.nst], (k / a.nst) & 1, a.wait_ns))
         waited = k + 1;
       else if (lane == 0)
         misc[2] = 1;
@@ -860,7 +865,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
   // lands in shared memory after the CTA is gone.
   if (misc[2] && warp == 0 && lane == 0) {
     const int issued = misc[1];
-    for (int k = waited; k < issued; ++k) (void)mbar_wait(&full[k % a.nst], (k / a.nst) & 1, 20000000ull);
+    for (int k = waited; k < issued; ++k)
+      (void)mbar_wait(&full[k % a.nst], (k / a.nst) & 1, (a.wait_ns < 20000000ull ? a.wait_ns : 20000000ull));
   }
   }  // !TR
 }
@@ -873,21 +879,13 @@ int64_t persist_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int sms) {
 using PersistKernel = void (*)(PagedArgs);
 
 // The kernel for (D, REP, KIND): up to four query heads per KV head take the transposed consumers, eight the
-// head-major ones. FP8 converts on the conversion unit (CONV 0) unless BPT_PAGED_CONV picks another split.
+// head-major ones. FP8 keys and values convert on the conversion unit (CONV 0) at D 128 with two query heads per
+// KV head (the configs' shape, where that measured fastest), on the integer pipe (CONV 3) elsewhere.
 template <int D, int REP, int KIND>
 PersistKernel persist_kernel() {
   if constexpr (REP <= 4) {
-    if constexpr (KIND == BPT_KV_FP8) {
-      static const int conv = env_int("BPT_PAGED_CONV", 0);
-      if constexpr (D == 128 && REP == 2) {
-        if (conv == 0) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 0>;
-        if (conv == 1) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 1>;
-        if (conv == 2) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 2>;
-      }
-      return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 3>;
-    } else {
-      return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 0>;
-    }
+    if constexpr (KIND == BPT_KV_FP8 && !(D == 128 && REP == 2)) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 3>;
+    return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 0>;
   } else {
     return paged_attn_persistent_kernel<D, REP, KIND, 0, false, 0>;
   }
@@ -896,7 +894,10 @@ PersistKernel persist_kernel() {
 template <int D, int REP, int KIND>
 int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   PagedArgs a = a0;
-  a.early = (flags & BPT_FLAG_PDL) && (flags & BPT_FLAG_KV_READY) ? 1 : 0;
+  a.stall = (flags & BPT_FLAG_TEST_STALL) ? 1 : 0;
+  a.wait_ns = a.stall ? kTestWaitNs : kWaitNs;
+  // (the stall test needs every issued copy awaited in order: no early copies before the dependency wait)
+  a.early = (flags & BPT_FLAG_PDL) && (flags & BPT_FLAG_KV_READY) && !a.stall ? 1 : 0;
   const int q_esize = a.q_dtype == BPT_DTYPE_F32 ? 4 : 2;
   const PersistLayout lay = persist_layout<D, 0>(a.Hkv, a.Hq, q_esize, a.scale_bytes);
   const int G = a.persist_ctas;
@@ -904,7 +905,7 @@ int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   const int fixed = 4 * (2 * a.B + 1) + 12 * a.max_cta_pages + 16 + 16 + a.Hkv * 32 * 4 * 4;
   // six stages of one page (32 KB for 8 KV heads at D 128) where they fit: config 2 measured 40.5, 37.3 and 37.0 us
   // per call at 4, 5 and 6
-  a.nst = max(2, min(min(env_int("BPT_PAGED_STAGES", 6), 8), (kMaxSmemPerCta - fixed) / (lay.stage_bytes + 16)));
+  a.nst = max(2, min(kPersistStages, (kMaxSmemPerCta - fixed) / (lay.stage_bytes + 16)));
   const int smem = a.nst * (lay.stage_bytes + 16) + fixed;
   const PersistKernel kernel = persist_kernel<D, REP, KIND>();
   int st = set_max_smem(reinterpret_cast<const void*>(kernel), smem);

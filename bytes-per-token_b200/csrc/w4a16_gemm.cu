@@ -240,24 +240,19 @@ int w4a16_gemm(const void* x, int64_t ldx, const int32_t* qweight, const void* s
   a.group = int(group);
   a.G = int(K / group);
   a.ZW = (a.G + 7) / 8;
-  // M tile and pipeline depth: 32-row tiles double the CTAs for M <= 64 (the N tiles alone leave SMs idle)
-  static const int bm_env = std::getenv("BPT_GEMM_BM") ? std::atoi(std::getenv("BPT_GEMM_BM")) : 0;
-  static const int st_env = std::getenv("BPT_GEMM_STAGES") ? std::atoi(std::getenv("BPT_GEMM_STAGES")) : 0;
-  const int bm = bm_env ? bm_env : (M <= 64 ? 32 : 64);
-  const int stages = st_env ? st_env : (bm == 32 ? 6 : 3);  // the measured best per tile
+  // M tile and pipeline depth: 32-row tiles double the CTAs for M <= 64 (the N tiles alone leave SMs idle); six stages
+  // for 32-row tiles, three for 64 (the measured best per tile)
+  const int bm = M <= 64 ? 32 : 64;
   const void* kernel = nullptr;
   int smem = 0;
 #define BPT_GEMM_PICK(F, B, S)                                                              \
-  if (fused == F && bm == B && stages == S) {                                               \
+  if (fused == F && bm == B) {                                                              \
     kernel = reinterpret_cast<const void*>(w4a16_gemm_kernel<F, B, S>);                    \
     smem = S * stage_bytes<B>() + kBN * a.G * 8;                                             \
   }
-  BPT_GEMM_PICK(false, 32, 3) BPT_GEMM_PICK(false, 32, 4) BPT_GEMM_PICK(false, 32, 6)
-  BPT_GEMM_PICK(false, 64, 3) BPT_GEMM_PICK(false, 64, 4) BPT_GEMM_PICK(false, 64, 6)
-  BPT_GEMM_PICK(true, 32, 3) BPT_GEMM_PICK(true, 32, 4) BPT_GEMM_PICK(true, 32, 6)
-  BPT_GEMM_PICK(true, 64, 3) BPT_GEMM_PICK(true, 64, 4) BPT_GEMM_PICK(true, 64, 6)
+  BPT_GEMM_PICK(false, 32, 6) BPT_GEMM_PICK(false, 64, 3) BPT_GEMM_PICK(true, 32, 6) BPT_GEMM_PICK(true, 64, 3)
 #undef BPT_GEMM_PICK
-  if (!kernel) return set_error(BPT_ERR_UNSUPPORTED, "w4a16 gemm: no kernel for tile %d x %d stages", bm, stages);
+  if (!kernel) return set_error(BPT_ERR_UNSUPPORTED, "w4a16 gemm: no kernel for a %d-row tile", bm);
   int st = set_max_smem(kernel, smem);
   if (st) return st;
   cudaLaunchConfig_t cfg = {};

@@ -243,16 +243,11 @@ int w4a16_gemm(const void* x, int64_t ldx, const int32_t* qweight, const void* s
 // The kernel for a shape: M >= 16 the tcgen05 GEMM (w4a16_tc.cu), else the mma.sync tiled GEMM (w4a16_gemm.cu);
 // M <= 8 the persistent streaming GEMV (w4a16_stream.cu); otherwise the tensor-core GEMV (w4a16_mma.cu) where
 // its staging fits, the CUDA-core kernel below last. The bulk-copy kernels need 16-byte aligned scales and zero
-// points. (BPT_W4A16_NO_TC, BPT_W4A16_NO_STREAM and BPT_W4A16_CUDA_CORES in the environment leave kernels out,
-// for comparisons.)
+// points.
 int w4a16_pick(int64_t M, int64_t N, int64_t K, int64_t group, bool zeros, bool aligned) {
-  static const bool cuda_cores = std::getenv("BPT_W4A16_CUDA_CORES") != nullptr;
-  static const bool no_tc = std::getenv("BPT_W4A16_NO_TC") != nullptr;
-  static const bool no_stream = std::getenv("BPT_W4A16_NO_STREAM") != nullptr;
-  if (cuda_cores) return BPT_W4A16_KERNEL_CUDA_CORES;
-  if (!no_tc && w4a16_tc_applies(M, N, K, group)) return BPT_W4A16_KERNEL_TCGEN05;
+  if (w4a16_tc_applies(M, N, K, group)) return BPT_W4A16_KERNEL_TCGEN05;
   if (w4a16_gemm_applies(M, N, K, group)) return BPT_W4A16_KERNEL_MMA_GEMM;
-  if (aligned && !no_stream && w4a16_stream_applies(M, N, K, group, zeros)) return BPT_W4A16_KERNEL_STREAM;
+  if (aligned && w4a16_stream_applies(M, N, K, group, zeros)) return BPT_W4A16_KERNEL_STREAM;
   if (aligned && w4a16_mma_applies(M, N, K, group)) return BPT_W4A16_KERNEL_MMA_GEMV;
   return BPT_W4A16_KERNEL_CUDA_CORES;
 }

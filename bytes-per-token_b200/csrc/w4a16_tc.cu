@@ -59,6 +59,8 @@ struct TcArgs {
   int ns;      // code and x ring stages
   int na;      // A ring stages (tensor memory, after the accumulator's BN columns)
   int gc;      // scale-table groups per CTA (an upper bound over the slices)
+  int stall;         // BPT_FLAG_TEST_STALL: the first CTA issues no code tile from chunk 1 on (bounded-wait tests)
+  uint64_t wait_ns;  // limit of the dequantizers' waits for code tiles
 };
 
 struct TcLayout {
@@ -247,7 +249,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (producer lane) the code tile of chunk c into stage rc.s; a refill (c >= ns) first waits for the release of
   // the stage's previous lap
   Ring rc;
+  const bool stall_here = a.stall && blockIdx.x == 0 && blockIdx.y == 0;
   auto issue_codes = [&](int c) {
+    // BPT_FLAG_TEST_STALL: the first CTA stops before chunk 1 (chunk 0 when it has one). The dequantizers await
+    // every tile issued before it, in order, so no copy is left in flight; their waits for the rest run out.
+    if (stall_here && c >= min(1, a.chunks - 1)) return false;
     if (c >= a.ns && !mbar_wait_sleep(&cempty[rc.s], rc.lap ^ 1u, 32u)) return false;
     mbar_arrive_expect_tx(&cfull[rc.s], kCBytes);
     tma_load_2d_hint(cbuf + rc.s * kCBytes, &tm_codes, (c0 + c) * (kChunkK / 8), n0, &cfull[rc.s], policy);
@@ -329,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int gl = 0, sub = (c0 * kChunkK % a.group) / kChunkK;  // the chunk's group (table row) and place in it
     Ring rc, ra;
     for (int c = 0; c < a.chunks; ++c, rc.next(a.ns), ra.next(a.na)) {
-      ok = mbar_wait(&cfull[rc.s], rc.lap) && ok;
+      ok = mbar_wait(&cfull[rc.s], rc.lap, a.wait_ns) && ok;
       const uint4 w = *reinterpret_cast<const uint4*>(cbuf + rc.s * kCBytes + r * 32 + 16 * h);
       __syncwarp();
       if (lane == 0) mbar_arrive(&cempty[rc.s]);
@@ -543,6 +549,8 @@ int w4a16_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
   a.ns = plan.ns;
   a.na = plan.na;
   a.gc = plan.gc;
+  a.stall = (flags & BPT_FLAG_TEST_STALL) ? 1 : 0;
+  a.wait_ns = a.stall ? kTestWaitNs : kWaitNs;
   const void* kernel = nullptr;
 #define BPT_TC_PICK(F, B) \
   if (fused == F && plan.bn == B) kernel = reinterpret_cast<const void*>(w4a16_tc_kernel<F, B>);

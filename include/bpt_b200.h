@@ -50,6 +50,13 @@ extern "C" {
  * pools are not written by the kernel this launch follows, so the kernel maps its pages and starts their copies
  * before it waits on that kernel (q, the output and the workspace are still touched only after the wait). */
 #define BPT_FLAG_KV_READY 2
+/* For tests of the bounded device waits only. The launch's first CTA stops issuing its copies partway (every copy
+ * it did issue is still awaited, so nothing is left in flight), the waits that then find no data give up after
+ * ~2 ms instead of ~200 ms, the call records device error 1 (a bounded wait ran out; bpt_device_error) and its
+ * outputs are undefined. Taken by bpt_paged_attend / bpt_paged_attend_noalloc where they run the persistent kernel
+ * (it turns BPT_FLAG_KV_READY off) and by bpt_w4a16_linear / bpt_w4a16_gate_up_silu where they run the tcgen05
+ * GEMM; every other launch ignores it. */
+#define BPT_FLAG_TEST_STALL 0x40000000
 
 int bpt_abi_version(void);
 const char* bpt_last_error(void);
@@ -153,9 +160,12 @@ int bpt_paged_attend(const void* q, int q_dtype, int64_t q_stride_b, int64_t q_s
  * variable of this library: every GPU that loads the library holds it until the process exits. A call needs
  * 256 KiB + S * Hq * (D + 1) * 4 bytes of it (rounded up to 256 B per part), S = B + the GPU's SM count for
  * contiguous q with D 64 or 128 and Hkv <= 8, S = B * n_splits otherwise, and returns BPT_ERR_WORKSPACE,
- * launching nothing, when that is more. The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress) with that device current; make that first call before any stream
- * capture. Each call clears the tickets it uses (an asynchronous memset on `stream`) before the kernel.
+ * launching nothing, when that is more. The array used is the current device's: q (and every other tensor) must be
+ * memory of the current device (BPT_ERR_INVALID otherwise). The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current, and looks it up again when the device's current
+ * context has changed (after a cudaDeviceReset, say); make that first call before any stream capture. Each call
+ * clears the tickets it uses (an asynchronous memset on `stream`) before the kernel, so BPT_FLAG_PDL and
+ * BPT_FLAG_KV_READY give no overlap with the previous kernel here (the memset sits between them).
  * All calls on a device share the array: calls that overlap on the GPU (concurrent streams) race and corrupt
  * each other's results. Nothing here calls cudaMalloc, cudaFree or any allocating routine. */
 #define BPT_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)

@@ -139,6 +139,32 @@ def w4a16_linear(
     return y.to(x.dtype)
 
 
+def w4a16_gate_up_silu(
+    x: torch.Tensor,
+    qweight: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor | None,
+    group: int = 128,
+    dense_bf16: bool = False,
+) -> torch.Tensor:
+    """silu(g) * u for a fused gate/up weight whose rows alternate gate (2i) and up (2i + 1), in x's dtype.
+
+    The MLP of `src/fastserve/engine/model.py:95-96` (`down(silu(gate(x)) * up(x))`) up to its input of down_proj,
+    with g and u kept in fp32 from the fp32-accumulated matmul (`w4a16_linear` above, before its final rounding)
+    and one rounding at the end: the arithmetic that fp32 accumulation prescribes. The reference model rounds g
+    and u to bf16 first (its nn.Linear outputs); that rounding is left out here on purpose.
+    """
+    n, k = qweight.shape[0], qweight.shape[1] * 8
+    codes = unpack_nibbles_int32(qweight, k)
+    zeros = None if qzeros is None else unpack_nibbles_int32(qzeros, k // group)
+    w = dequantize_w4a16(codes, scales, zeros, group)
+    if dense_bf16:
+        w = w.to(torch.bfloat16).float()
+    y = torch.nn.functional.linear(x.float(), w)
+    g, u = y[..., 0::2], y[..., 1::2]
+    return (torch.nn.functional.silu(g) * u).to(x.dtype)
+
+
 def pack_w4a16(codes: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor):
     """(codes, scales, zeros) -> the stored tensors (qweight, scales, qzeros)."""
     return pack_nibbles_int32(codes), scales.contiguous(), pack_nibbles_int32(zeros)

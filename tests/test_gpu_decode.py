@@ -17,40 +17,50 @@ from oracle import w4a16 as ow4
 pytestmark = pytest.mark.gpu
 
 
-def dequant(t):
+TOL = {"atol": 1e-2, "rtol": 1e-2}  # the north star's bf16 tolerance
+
+
+def dequant(t, dense_bf16=False):
+    """The layer's dense weight: s (q - z) in fp32, or rounded once to bf16 as the reference model holds it after
+    quant/compressed.py:56-69 (what the tcgen05 GEMM multiplies with at M >= 16)."""
     qweight, scales, qzeros = [x.cpu() for x in t]
     n, k = qweight.shape[0], qweight.shape[1] * 8
     g = k // scales.shape[1]
     codes = ow4.unpack_nibbles_int32(qweight, k)
     zeros = ow4.unpack_nibbles_int32(qzeros, k // g)
-    return ow4.dequantize_w4a16(codes, scales, zeros, g)
+    w = ow4.dequantize_w4a16(codes, scales, zeros, g)
+    return w.to(torch.bfloat16).float() if dense_bf16 else w
 
 
 def linear(x, w):  # the reference's fp32 linear over the dequantized weight, rounded once to bf16
     return (x.float() @ w.T).to(torch.bfloat16)
 
 
-def reference_layer(dec, layer, h, cos, sin, lengths_after, kpool, vpool):
+def reference_layer(dec, layer, h, cos, sin, lengths_after, kpool, vpool, dense_bf16=False):
     """engine/model.py's DecoderLayer.forward for one token, on the CPU, over the given pools."""
     from bpt_b200.decode import rms_norm, rope_apply
 
     d = dec.dims
     b = h.shape[0]
     qd, kd = d.q_heads * d.head_dim, d.kv_heads * d.head_dim
+
+    def weight(t):
+        return dequant(t, dense_bf16)
+
     x = rms_norm(h, layer.input_norm.cpu(), d.eps)
-    qkv = linear(x, dequant(layer.qkv))
+    qkv = linear(x, weight(layer.qkv))
     q = rms_norm(qkv[:, :qd].view(b, d.q_heads, d.head_dim), layer.q_norm.cpu(), d.eps)
     k = rms_norm(qkv[:, qd : qd + kd].view(b, d.kv_heads, d.head_dim), layer.k_norm.cpu(), d.eps)
     v = qkv[:, qd + kd :].view(b, d.kv_heads, d.head_dim)
     q, k = rope_apply(q, cos, sin), rope_apply(k, cos, sin)
     kv = okv.PagedKV("fp8", kpool, vpool, layer.kv.k_scale, layer.kv.v_scale, dec.block_table.cpu(), 16)
     attn = oatt.paged_attend(q.float(), kv, lengths_after, 1.0 / math.sqrt(d.head_dim)).to(torch.bfloat16)
-    h = h + linear(attn.reshape(b, qd), dequant(layer.o))
+    h = h + linear(attn.reshape(b, qd), weight(layer.o))
     x = rms_norm(h, layer.post_norm.cpu(), d.eps)
-    gu = dequant(layer.gate_up)
+    gu = weight(layer.gate_up)
     g, u = (x.float() @ gu[0::2].T), (x.float() @ gu[1::2].T)
     act = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)
-    return h + linear(act, dequant(layer.down)), k, v
+    return h + linear(act, weight(layer.down)), k, v
 
 
 def test_decode_step_layers_match_reference():
@@ -81,9 +91,38 @@ def test_decode_step_layers_match_reference():
             before_k[wb[i], wo[i]] = kpool[wb[i], wo[i]]
             before_v[wb[i], wo[i]] = vpool[wb[i], wo[i]]
         assert torch.equal(before_k, kpool) and torch.equal(before_v, vpool)
-        err = (got.cpu().float() - want.float()).norm() / want.float().norm()
-        assert err < 2e-2, err
+        torch.testing.assert_close(got.cpu().float(), want.float(), **TOL)
         h = got
+
+
+def test_fused_decode_step_batch64_matches_reference():
+    """Config 5's benchmarked path: batch 64, so every linear runs on the tcgen05 GEMM, with the fused norm / RoPE
+    / KV-write kernels, at Qwen3-1.7B's widths (two layers). The residual stream after the last layer of one eager
+    step against the reference's layers on the CPU (dense bf16 weights, as the tcgen05 GEMM multiplies), atol / rtol
+    1e-2. (The residual stream, not the final-normed output: the final RMSNorm divides by the stream's RMS and so
+    scales the bf16 rounding of elements that nearly cancel into differences of several bf16 steps.)"""
+    from bpt_b200.decode import Qwen3Decoder, Qwen3Dims, rope_cos_sin
+    from bpt_b200.kernels.w4a16 import w4a16_kernel
+
+    dims = Qwen3Dims(layers=2, vocab=512)
+    g = torch.Generator().manual_seed(64)
+    lengths = torch.randint(16, 300, (64,), generator=g)
+    dec = Qwen3Decoder(dims, lengths, seed=4, capacity=4, fused=True)
+    qkv_rows = (dims.q_heads + 2 * dims.kv_heads) * dims.head_dim
+    for n, k in ((qkv_rows, dims.hidden), (dims.hidden, dims.q_heads * dims.head_dim),
+                 (2 * dims.intermediate, dims.hidden), (dims.hidden, dims.intermediate)):
+        assert w4a16_kernel(64, n, k, dims.group) == "tcgen05"
+    dec.tokens.copy_(torch.randint(0, dims.vocab, (64,), generator=g))
+    pos = dec.lengths.to(torch.int64)
+    cos, sin = rope_cos_sin(pos, dims.head_dim, dims.rope_theta, torch.bfloat16)  # as step_body computes them
+    lengths_after = (dec.lengths + 1).cpu()
+    h = dec.embed[dec.tokens].cpu()
+    dec.step()  # eager: embed, 2 fused layers, final norm, LM head
+    torch.cuda.synchronize()
+    for layer in dec.layers:  # each layer's pool now holds the token this step wrote
+        h, _, _ = reference_layer(dec, layer, h, cos.cpu(), sin.cpu(), lengths_after, layer.kv.k_pool.cpu(),
+                                  layer.kv.v_pool.cpu(), dense_bf16=True)
+    torch.testing.assert_close(dec.h.cpu().float(), h.float(), **TOL)  # the fused path's residual stream
 
 
 def test_decode_step_graph_replay_equals_eager():
@@ -182,6 +221,5 @@ def test_fused_decode_step_matches_unfused():
         plain.step()
         fused.step()
     torch.cuda.synchronize()
-    a, b = plain.hidden.float(), fused.hidden.float()
-    assert ((a - b).norm() / a.norm()).item() < 2e-2
+    torch.testing.assert_close(fused.hidden.float(), plain.hidden.float(), **TOL)
     assert torch.equal(plain.lengths, fused.lengths)

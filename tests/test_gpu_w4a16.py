@@ -63,6 +63,18 @@ def check_linear(m, n, k, group, seed=0, symmetric=False):
     assert err <= 2 ** -8 * exact.abs().max().item() + 1e-6
 
 
+def check_gate_up(got, x, fused, group=128):
+    """The fused gate_up + SwiGLU output against silu(g) * u of the fp32 sums (g and u not rounded, one rounding at
+    the end), the arithmetic of the kernel a shape takes, at the north star's atol / rtol 1e-2."""
+    from bpt_b200.kernels.w4a16 import w4a16_kernel
+
+    m, k = x.shape
+    n = fused[0].shape[0]
+    dense_bf16 = w4a16_kernel(m, n, k, group) == "tcgen05"
+    want = ow4.w4a16_gate_up_silu(x, *[t.cpu() for t in fused], group, dense_bf16=dense_bf16)
+    torch.testing.assert_close(got.cpu().float(), want.float(), **TOL)
+
+
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 16])
 def test_linear_config1_shape(m):
     check_linear(m, 6144, 2048, 128, seed=m)
@@ -96,9 +108,7 @@ def test_gemm_gate_up_silu():
     qg, qu = quantize_w4a16(gate.cuda()), quantize_w4a16(up.cuda())
     fused = [interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)]
     got = w4a16_gate_up_silu(x.cuda(), *fused)
-    g = ow4.w4a16_linear(x, *[t.cpu() for t in qg], 128).float()
-    u = ow4.w4a16_linear(x, *[t.cpu() for t in qu], 128).float()
-    torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
+    check_gate_up(got, x, fused)
 
 
 def test_m16_long_k_splits_k_over_a_cluster():
@@ -117,10 +127,8 @@ def test_small_n_splits_k_and_matches():
     gate, up = dense(128, 2048, 31), dense(128, 2048, 32)
     x = acts(3, 2048, 33)
     qg, qu = quantize_w4a16(gate.cuda()), quantize_w4a16(up.cuda())
-    got = w4a16_gate_up_silu(x.cuda(), *[interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)])
-    g = ow4.w4a16_linear(x, *[t.cpu() for t in qg], 128).float()
-    u = ow4.w4a16_linear(x, *[t.cpu() for t in qu], 128).float()
-    torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
+    fused = [interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)]
+    check_gate_up(w4a16_gate_up_silu(x.cuda(), *fused), x, fused)
 
 
 @pytest.mark.parametrize("m,n,k,group", [(1, 16, 256, 64), (2, 4096, 2048, 32), (8, 2048, 6144, 128),
@@ -181,11 +189,7 @@ def test_gate_up_silu_matches_two_linears():
         x = acts(m, k, 5 + m)
         qg, qu = quantize_w4a16(gate.cuda()), quantize_w4a16(up.cuda())
         fused = [interleave_rows(a, b) for a, b in zip(qg, qu, strict=True)]
-        got = w4a16_gate_up_silu(x.cuda(), *fused)
-        g = ow4.w4a16_linear(x, *[t.cpu() for t in qg], 128).float()
-        u = ow4.w4a16_linear(x, *[t.cpu() for t in qu], 128).float()
-        # the reference rounds gate and up to bf16 before silu; the fused kernel keeps fp32 throughout
-        torch.testing.assert_close(got.cpu().float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=2e-2)
+        check_gate_up(w4a16_gate_up_silu(x.cuda(), *fused), x, fused)
 
 
 def test_out_buffer_views_and_pdl():
@@ -237,3 +241,32 @@ def test_pack_quantized_checkpoint_serves_without_a_dense_copy(m):
     torch.testing.assert_close(got, torch.nn.functional.linear(x.float(), dense.float()), **TOL)
     own = ow4.w4a16_linear(x, qweight, scales, None, group, dense_bf16=w4a16_kernel(m, n, k, group, False) == "tcgen05")
     torch.testing.assert_close(got, own.float(), **TOL)
+
+
+def test_unaligned_scales_take_the_cuda_core_kernel():
+    """Scales that are not 16-byte aligned cannot arrive by bulk copy: the CUDA-core kernel takes the shape, with the
+    same group-sum arithmetic."""
+    from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_linear
+
+    n, k = 512, 2048
+    w = dense(n, k, 70)
+    qweight, scales, qzeros = quantize_w4a16(w.cuda())
+    store = torch.empty(scales.numel() + 1, dtype=torch.float16, device="cuda")
+    shifted = store[1:].view_as(scales)  # 2 bytes past a 16-byte boundary
+    shifted.copy_(scales)
+    assert shifted.data_ptr() % 16 != 0
+    for m in (1, 3):
+        x = acts(m, k, 71 + m)
+        got = w4a16_linear(x.cuda(), qweight, shifted, qzeros)
+        want = ow4.w4a16_linear(x, qweight.cpu(), scales.cpu(), qzeros.cpu(), 128)
+        torch.testing.assert_close(got.cpu().float(), want.float(), **TOL)
+
+
+def test_long_k_many_rows_takes_the_mma_gemm():
+    """A shape whose per-CTA scale table does not fit the tcgen05 kernel's shared memory (K = 16384 at group 64,
+    enough row tiles that K is not split) goes to the mma.sync GEMM."""
+    from bpt_b200.kernels.w4a16 import w4a16_kernel
+
+    m, n, k, group = 256, 4864, 16384, 64
+    assert w4a16_kernel(m, n, k, group) == "mma_gemm"
+    check_linear(m, n, k, group, seed=80)

@@ -61,6 +61,48 @@ def test_no_alloc_attend_matches_the_workspace_entry_point_on_two_calls(kind):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("variant", ["16 KV heads", "strided q"])
+def test_no_alloc_split_kernel_branch_matches_on_two_calls(variant):
+    """Shapes the persistent kernel does not take (more than 8 KV heads; q rows with a head stride other than D)
+    run the split kernels with per-sequence tickets: the same two-call check against the workspace entry point."""
+    import dataclasses
+
+    from bpt_b200 import _lib, workloads
+    from bpt_b200.kernels.kv_attention import attend
+
+    lengths = [500, 3, 260]
+    hkv = 16 if variant == "16 KV heads" else 8
+    case = workloads.paged_case("fp8", 3, 16, hkv, 128, lengths, 16, 64, seed=31, device="cuda")
+    if variant == "strided q":
+        wide = torch.zeros(3, 16, 256, dtype=case.q.dtype, device="cuda")
+        wide[..., :128] = case.q
+        case = dataclasses.replace(case, q=wide[..., :128])
+        assert case.q.stride(1) == 256
+    scale = 1.0 / math.sqrt(128)
+    split, tokens = 64, max(lengths)
+    want = attend(case.q, case.kv, case.lengths, scale, split=split, tokens=tokens)
+    for _ in range(2):
+        out = torch.full_like(want, float("nan"))
+        assert call_noalloc(case, scale, split, -(-tokens // split), out) == _lib.OK, _lib.lib().bpt_last_error()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out, want, rtol=2e-4, atol=2e-4 * want.abs().max().item())
+    assert _lib.device_error() == 0
+
+
+def test_no_alloc_refuses_tensors_of_another_device_than_the_current_one():
+    """The array used is the current device's: host memory passed as q is refused before anything launches."""
+    from bpt_b200 import _lib, workloads
+
+    case = workloads.paged_case("fp8", 2, 16, 8, 128, [40, 17], 16, 8, seed=4, device="cuda")
+    host_q = case.q.cpu().pin_memory()
+    import dataclasses
+
+    out = torch.zeros(2, 16, 128, device="cuda")
+    status = call_noalloc(dataclasses.replace(case, q=host_q), 0.1, 16, 3, out)
+    assert status == _lib.ERR_INVALID
+    assert out.abs().sum() == 0
+
+
 def test_no_alloc_refuses_a_request_beyond_its_fixed_scratch():
     from bpt_b200 import _lib, workloads
 
