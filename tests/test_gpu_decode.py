@@ -97,14 +97,18 @@ def test_decode_step_layers_match_reference():
 
 def test_fused_decode_step_batch64_matches_reference():
     """Config 5's benchmarked path: batch 64, so every linear runs on the tcgen05 GEMM, with the fused norm / RoPE
-    / KV-write kernels, at Qwen3-1.7B's widths (two layers). The residual stream after the last layer of one eager
-    step against the reference's layers on the CPU (dense bf16 weights, as the tcgen05 GEMM multiplies), atol / rtol
-    1e-2. (The residual stream, not the final-normed output: the final RMSNorm divides by the stream's RMS and so
-    scales the bf16 rounding of elements that nearly cancel into differences of several bf16 steps.)"""
+    / KV-write kernels, at Qwen3-1.7B's widths. The residual stream after one decoder layer of an eager step against
+    the reference's layer on the CPU (dense bf16 weights, as the tcgen05 GEMM multiplies), atol / rtol 1e-2.
+
+    One layer, compared from the same input: the synthetic pools hold uniformly random E4M3 codes (keys up to
+    +-7), so the softmax is sharply peaked and a one-ulp difference in a later layer's input moves its attention
+    far more than any kernel error; chaining layers would compare that amplification, not the kernels. (The
+    residual stream, not the final-normed output, for the same reason: the final RMSNorm rescales the rounding of
+    nearly cancelling elements.)"""
     from bpt_b200.decode import Qwen3Decoder, Qwen3Dims, rope_cos_sin
     from bpt_b200.kernels.w4a16 import w4a16_kernel
 
-    dims = Qwen3Dims(layers=2, vocab=512)
+    dims = Qwen3Dims(layers=1, vocab=512)
     g = torch.Generator().manual_seed(64)
     lengths = torch.randint(16, 300, (64,), generator=g)
     dec = Qwen3Decoder(dims, lengths, seed=4, capacity=4, fused=True)
@@ -117,12 +121,12 @@ def test_fused_decode_step_batch64_matches_reference():
     cos, sin = rope_cos_sin(pos, dims.head_dim, dims.rope_theta, torch.bfloat16)  # as step_body computes them
     lengths_after = (dec.lengths + 1).cpu()
     h = dec.embed[dec.tokens].cpu()
-    dec.step()  # eager: embed, 2 fused layers, final norm, LM head
+    dec.step()  # eager: embed, the fused layer, final norm, LM head
     torch.cuda.synchronize()
-    for layer in dec.layers:  # each layer's pool now holds the token this step wrote
-        h, _, _ = reference_layer(dec, layer, h, cos.cpu(), sin.cpu(), lengths_after, layer.kv.k_pool.cpu(),
-                                  layer.kv.v_pool.cpu(), dense_bf16=True)
-    torch.testing.assert_close(dec.h.cpu().float(), h.float(), **TOL)  # the fused path's residual stream
+    layer = dec.layers[0]  # its pool now holds the token this step wrote
+    want, _, _ = reference_layer(dec, layer, h, cos.cpu(), sin.cpu(), lengths_after, layer.kv.k_pool.cpu(),
+                                 layer.kv.v_pool.cpu(), dense_bf16=True)
+    torch.testing.assert_close(dec.h.cpu().float(), want.float(), **TOL)  # the fused path's residual stream
 
 
 def test_decode_step_graph_replay_equals_eager():
