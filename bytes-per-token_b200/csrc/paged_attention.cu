@@ -545,7 +545,8 @@ int64_t split_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t n_splits
 
 bool persistent_applies(const PagedArgs& a, int64_t D, int64_t& cap) {
   const int G = num_sms();
-  cap = (int64_t(a.B) * a.bt_stride + G - 1) / G;
+  // a CTA owns at most W pages, W = ceil((pages + kStartCost B) / CTAs) (the cost-weighted split)
+  cap = (int64_t(a.B) * a.bt_stride + int64_t(kStartCost) * a.B + G - 1) / G;
   return (D == 64 || D == 128) && a.Hkv <= kMmaMaxHkv &&
          a.B <= kPersistMaxSeqs && cap <= kPersistMaxCtaPages && a.q_sh == D && a.q_sb == a.Hq * D &&
          aligned16(a.q);

@@ -1,8 +1,9 @@
 // Persistent, warp-specialized paged decode attention with the split merge fused in (included by
 // paged_attention.cu, inside its namespace; uses the MMA helpers of paged_attention_mma.cuh).
 //
-// Work split. The pages of all sequences, laid end to end, are cut into one equal contiguous range per CTA
-// (one CTA per SM), so ragged lengths never unbalance the GPU. The piece of a sequence that falls inside one
+// Work split. The pages of all sequences, laid end to end, are cut into one contiguous range per CTA (one CTA per
+// SM) of equal cost, a page costing 1 and a sequence's first page kStartCost more, so ragged lengths never
+// unbalance the GPU and a range that opens a sequence takes fewer pages. The piece of a sequence that falls inside one
 // CTA's range is a "part": it has its own online-softmax state and leaves one partial (out, lse). A
 // sequence's parts are the CTAs first_b .. last_b whose ranges meet it; part (c, b) writes workspace slot
 // c + b, so a launch needs at most #CTAs + B slots. The CTA that finishes a sequence's last part merges its
@@ -22,6 +23,11 @@ constexpr int kPersistMaxSeqs = 4096;
 constexpr int kMaxSmemPerCta = 227 * 1024;  // sm_100 opt-in dynamic shared memory per block
 constexpr int kPersistMaxCtaPages = 4096;
 constexpr int kPersistStages = 6;
+// Each sequence's first page carries this many pages' worth of extra cost in the work split (the part it opens
+// costs a q copy, a partial, a ticket and shorter steps at its edges): CTA ranges cut the cost evenly, not the
+// page count, so a CTA whose range holds a sequence start gets correspondingly fewer pages.
+constexpr int kStartCost = 2;
+
 constexpr int64_t kCounterBytesP = 65536 * 4;  // the ticket counters, at the workspace's start (as paged_attend)
 
 struct PersistLayout {
@@ -49,6 +55,7 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(unsigned int* p, uint32
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
+
 
 __device__ __forceinline__ void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
@@ -408,8 +415,8 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
     if (!last) continue;
 
     // ---- end of a part: lane (g, c) holds head c at dims g*VD + [0, VD) ----
-    const int first_cta = off[b] / per;
-    const int last_cta = (off[b + 1] - 1) / per;
+    const int first_cta = (off[b] + kStartCost * (b + 1)) / per;  // the CTAs owning b's first and last pages
+    const int last_cta = (off[b + 1] - 1 + kStartCost * (b + 1)) / per;
     const int nparts = last_cta - first_cta + 1;
     if (c < REP) {
       const int hq = h * REP + c;
@@ -509,8 +516,22 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
   }
   __syncthreads();
   const int P = off[B];
-  const int per = (P + G - 1) / G;
-  const int g0 = min(P, cta * per), g1 = min(P, g0 + per);
+  // CTA c owns the pages whose cost position lies in [c W, (c + 1) W), W the total cost over the CTAs
+  const int per = (P + kStartCost * B + G - 1) / G;
+  // The first page whose cost position is >= t (P if none): sequence b's pages sit at positions p + kStartCost (b + 1),
+  // so with b the last sequence whose first position is <= t, it is t - kStartCost (b + 1) clamped to b's pages
+  // (past b's last page: the next page in order, whose position is above t). One binary search over sequences.
+  auto first_page_at = [&](int64_t t) -> int {
+    if (t < kStartCost) return 0;
+    int lo = 0, hi = B;  // invariant: start position of lo <= t (sequence 0's is kStartCost)
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (off[mid] + int64_t(kStartCost) * (mid + 1) <= t) lo = mid; else hi = mid;
+    }
+    const int64_t p = t - int64_t(kStartCost) * (lo + 1);
+    return int(min(int64_t(off[lo + 1]), max(int64_t(off[lo]), p)));
+  };
+  const int g0 = first_page_at(int64_t(cta) * per), g1 = first_page_at(int64_t(cta + 1) * per);
   const int n = g1 - g0;
   for (int k = tid; k < n; k += blockDim.x) {
     const int gp = g0 + k;
@@ -554,9 +575,10 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
     for (int k = 0; k < n; ++k, st = (st + 1 == a.nst) ? 0 : st + 1, eph ^= (st == 0) ? 1u : 0u) {
       if (k == pre && pre > 0) q_copies_of_first_pages();
       if (misc[2]) break;
-      // BPT_FLAG_TEST_STALL: CTA 0 issues nothing from its second page on (its first, if it has one page). Every
-      // page it did issue is awaited by the consumers before they reach the missing one, so no copy is in flight.
-      if (a.stall && cta == 0 && k == min(1, n - 1)) break;
+      // BPT_FLAG_TEST_STALL: the CTA holding the first page issues nothing from its second page on (its first, if it
+      // has one page). Every page it did issue is awaited by the consumers before they reach the missing one, so
+      // no copy is in flight.
+      if (a.stall && g0 == 0 && k == min(1, n - 1)) break;
       if (k >= a.nst && !mbar_wait_warp(&empty[st], eph, a.wait_ns)) {
         misc[2] = 1;
         break;
@@ -819,8 +841,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
     if (!last) continue;
 
     // ---- end of a part: its partial, then the ticket; the last part of a sequence merges ----
-    const int first_cta = off[b] / per;
-    const int last_cta = (off[b + 1] - 1) / per;
+    const int first_cta = (off[b] + kStartCost * (b + 1)) / per;  // the CTAs owning b's first and last pages
+    const int last_cta = (off[b + 1] - 1 + kStartCost * (b + 1)) / per;
     const int nparts = last_cta - first_cta + 1;
     if (g < REP) {
       const int hq = h * REP + g;

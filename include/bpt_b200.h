@@ -50,8 +50,9 @@ extern "C" {
  * pools are not written by the kernel this launch follows, so the kernel maps its pages and starts their copies
  * before it waits on that kernel (q, the output and the workspace are still touched only after the wait). */
 #define BPT_FLAG_KV_READY 2
-/* For tests of the bounded device waits only. The launch's first CTA stops issuing its copies partway (every copy
- * it did issue is still awaited, so nothing is left in flight), the waits that then find no data give up after
+/* For tests of the bounded device waits only. One CTA of the launch (the one holding the first page, or the first
+ * weight tile) stops issuing its copies partway (every copy it did issue is still awaited, so nothing is left in
+ * flight), the waits that then find no data give up after
  * ~2 ms instead of ~200 ms, the call records device error 1 (a bounded wait ran out; bpt_device_error) and its
  * outputs are undefined. Taken by bpt_paged_attend / bpt_paged_attend_noalloc where they run the persistent kernel
  * (it turns BPT_FLAG_KV_READY off) and by bpt_w4a16_linear / bpt_w4a16_gate_up_silu where they run the tcgen05
