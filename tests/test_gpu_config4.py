@@ -54,8 +54,8 @@ def test_config4_linear_matches_oracle(name, m):
     kernel = w4a16_kernel(m, n, k, 128)
     if m >= 16:
         assert kernel == "tcgen05", kernel  # the benchmarked tensor-core path
-    elif m <= 8:
-        assert kernel == "stream", kernel
+    else:
+        assert kernel == "stream", kernel  # M <= 8: the persistent streaming GEMV
     got = w4a16_linear(x.cuda(), *gpu, group=128).cpu().float()
     want = torch.nn.functional.linear(x.float(), dense[kernel == "tcgen05"]).to(torch.bfloat16).float()
     torch.testing.assert_close(got, want, **TOL)

@@ -83,11 +83,16 @@ def test_decode_step_layers_match_reference():
         torch.cuda.synchronize()
         kpool, vpool = layer.kv.k_pool.cpu(), layer.kv.v_pool.cpu()
         want, k, v = reference_layer(dec, layer, h.cpu(), cos.cpu(), sin.cpu(), lengths_after.cpu(), kpool, vpool)
-        # the step wrote exactly this token's K and V codes, and nothing else
+        # the step wrote this token's K and V codes, and nothing else. The codes come from the GPU's own k and v,
+        # whose last bits can differ from the oracle's (the linear's rounding): a code may sit one E4M3 step from the
+        # oracle's store (the write itself is bit-exact from identical inputs: test_gpu_attention.py)
         wb, wo = write_blocks.cpu()[:, 0], write_offsets.cpu()[:, 0]
         for i in range(b):
-            assert torch.equal(kpool[wb[i], wo[i]], okv.fp8_store(k[i].float(), float(layer.kv.k_scale)))
-            assert torch.equal(vpool[wb[i], wo[i]], okv.fp8_store(v[i].float(), float(layer.kv.v_scale)))
+            for pool, ref, sc in ((kpool, k, layer.kv.k_scale), (vpool, v, layer.kv.v_scale)):
+                got_c, want_c = pool[wb[i], wo[i]], okv.fp8_store(ref[i].float(), float(sc))
+                assert (got_c == want_c).float().mean() > 0.97
+                step = okv.fp8_load(want_c, float(sc)).abs() / 8 + 2 ** -9 * float(sc)  # one E4M3 step, subnormals too
+                assert ((okv.fp8_load(got_c, float(sc)) - okv.fp8_load(want_c, float(sc))).abs() <= step * 1.01).all()
             before_k[wb[i], wo[i]] = kpool[wb[i], wo[i]]
             before_v[wb[i], wo[i]] = vpool[wb[i], wo[i]]
         assert torch.equal(before_k, kpool) and torch.equal(before_v, vpool)
