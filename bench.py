@@ -236,7 +236,7 @@ class Timer:
 # ---- our arm ------------------------------------------------------------------------------------------------------
 
 
-def build_inputs(device: torch.device, seed: int):
+def build_inputs(device: torch.device, seed: int, attention: bool = True):
     from bpt_b200 import workloads
     from bpt_b200.kernels.w4a16 import quantize_w4a16
 
@@ -246,7 +246,7 @@ def build_inputs(device: torch.device, seed: int):
         w = torch.randn(6144, 2048, generator=g, device=device) * 0.02
         weights.append(quantize_w4a16(w, 128))
     x = torch.randn(1, 2048, generator=g, device=device).to(torch.bfloat16)
-    attn = [workloads.config2(device=device, seed=seed * 100 + i) for i in range(ATTN_BATCHES)]
+    attn = [workloads.config2(device=device, seed=seed * 100 + i) for i in range(ATTN_BATCHES)] if attention else []
     return weights, x, attn
 
 
@@ -805,6 +805,36 @@ def run_case(args) -> None:
         y = torch.empty(1, 6144, dtype=torch.bfloat16, device=dev)
         us = _case_time(lambda i: w4a16_linear(case.x, case.qweight, case.scales, case.qzeros, out=y), args.launches)
         print(f"{name}: {us:.2f} us per launch")
+    elif name == "gemv-kernels":
+        # config 1 as the bench's chain (40 rotating weight copies, each call waiting on its predecessor under PDL)
+        # on the streaming tensor-core GEMV and on the CUDA-core kernel (packed fp32x2 FMAs over magic-number
+        # unpacked codes), which the public API takes when the scales and zero points are not 16-byte aligned
+        timer = Timer(dev, None)
+        weights, x, _ = build_inputs(dev, seed=0, attention=False)
+        y = torch.empty(1, 6144, dtype=torch.bfloat16, device=dev)
+
+        def unaligned(t):
+            buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=dev)
+            view = buf[1:].view_as(t)
+            view.copy_(t)
+            return view
+
+        variants = {"stream (aligned)": weights,
+                    "CUDA cores (unaligned scales)": [(qw, unaligned(sc), unaligned(qz)) for qw, sc, qz in weights]}
+        nbytes = workloads.w4a16_bytes(1, 6144, 2048)
+        print("| kernel | us per chained call | GB/s | of HBM peak |\n|---|---|---|---|")
+        for label, ws in variants.items():
+            assert (ws[0][1].data_ptr() % 16 == 0) == label.startswith("stream"), label
+
+            def call(i, ws=ws):
+                qw, sc, qz = ws[i % GEMV_COPIES]
+                w4a16_linear(x, qw, sc, qz, out=y, pdl=True)
+
+            for i in range(5):
+                call(i)
+            us = timer(call, 200) * 1e3 / 200
+            gbs = nbytes / us / 1e3
+            print(f"| {label} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} |", flush=True)
     elif name.startswith("gate-up-m"):
         m = int(name.split("-m")[1])
         g = torch.Generator(device=dev).manual_seed(0)
@@ -921,7 +951,7 @@ def run_case(args) -> None:
         raise SystemExit(f"unknown case {name!r}")
 
 
-CASES = ["attention-config2", "attention-config3", "gemv-config1", "gate-up-m16", "gate-up-m64", "gate-up-m256",
+CASES = ["attention-config2", "attention-config3", "gemv-config1", "gemv-kernels", "gate-up-m16", "gate-up-m64", "gate-up-m256",
          "norm-quant", "kivi-sweep", "kv-write-sweep", "norm-quant-sweep"]
 
 

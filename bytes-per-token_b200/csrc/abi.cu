@@ -1,5 +1,7 @@
 // Status reporting shared by every entry point: the thread-local error message, the device-side error flag,
 // and small cached device properties.
+#include <cudaTypedefs.h>
+
 #include <cstdarg>
 #include <cstdio>
 
@@ -39,6 +41,18 @@ int num_sms() {
     cache[dev] = n > 0 ? n : 148;
   }
   return cache[dev];
+}
+
+void* tensor_map_encoder() {
+  static void* fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return p;
+  }();
+  return fn;
 }
 
 int set_max_smem(const void* kernel, int bytes) {

@@ -25,6 +25,8 @@ int set_error(int status, const char* fmt, ...);
 int check_launch(const char* what);
 int num_sms();
 int set_max_smem(const void* kernel, int bytes);
+// The driver's cuTensorMapEncodeTiled (a PFN_cuTensorMapEncodeTiled_v12000), or null if the driver lacks it.
+void* tensor_map_encoder();
 
 #define BPT_REQUIRE(cond, status, ...)                 \
   do {                                                \
@@ -169,6 +171,22 @@ __device__ __forceinline__ void bulk_g2s_evict_first(void* smem_dst, const void*
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_u32(smem_dst)),
       "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses of shared memory (and those it acquired from other threads)
+// before its later async-proxy ones, e.g. reads of a ring stage before the bulk copy that overwrites it.
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 4-D tiled tensor copy global -> shared through the TMA engine with an L2 eviction hint, completing on `bar`.
+// `map` is a __grid_constant__ kernel parameter; the innermost coordinate times the element size must be a multiple
+// of 16 bytes.
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const void* map, int c0, int c1, int c2, int c3,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 

@@ -17,7 +17,11 @@
 // reference's kernel 2), or the merged attention: every CTA of a sequence with more than one split stores
 // its partial in the workspace, takes a ticket from an atomic counter, and the last one merges (exactly
 // reference.merge_partials) and resets the counter. No CTA ever waits on another.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <math_constants.h>
+
+#include <cstring>
 
 #include <algorithm>
 #include <cstdlib>

@@ -34,18 +34,34 @@ struct PersistLayout {
   int stage_bytes, kpitch, vpitch, kpage, vpage, q_off, q_bytes;
 };
 
+// COPY: how a page lands in its stage. 0: K and V pages as stored ([token][head][D], one bulk copy each); bits 0 / 1:
+// K / V token rows one by one to a 16-byte padded pitch; 4 (D = 128): K and V as 4-D tensor copies into head-major
+// tiles [head][token][128 bytes] with the 128-byte swizzle (16-byte chunk j of token row t at chunk j ^ (t mod 8)),
+// so the consumers' row reads meet no bank conflict with one copy per page (stages then start on 1 KB boundaries).
 template <int D, int COPY>
 __host__ __device__ inline PersistLayout persist_layout(int Hkv, int Hq, int q_esize, int scale_bytes) {
   PersistLayout p;
   const int rowb = Hkv * D;
-  p.kpitch = (COPY & 1) ? rowb + 16 : rowb;
-  p.vpitch = (COPY & 2) ? rowb + 16 : rowb;
-  p.kpage = kBS * p.kpitch;
-  p.vpage = kBS * p.vpitch;
+  p.kpitch = (COPY & 4) ? D : (COPY & 1) ? rowb + 16 : rowb;
+  p.vpitch = (COPY & 4) ? D : (COPY & 2) ? rowb + 16 : rowb;
+  p.kpage = (COPY & 4) ? kBS * rowb : kBS * p.kpitch;
+  p.vpage = (COPY & 4) ? kBS * rowb : kBS * p.vpitch;
   p.q_bytes = Hq * D * q_esize;
   p.q_off = p.kpage + p.vpage + 2 * scale_bytes;
-  p.stage_bytes = (p.q_off + p.q_bytes + 127) & ~127;
+  p.stage_bytes = (COPY & 4) ? (p.q_off + p.q_bytes + 1023) & ~1023 : (p.q_off + p.q_bytes + 127) & ~127;
   return p;
+}
+
+// Byte offset in a stage's K (or V) page of token t's 16-byte chunk j (bytes 16 j .. 16 j + 15 of the head's D)
+// for KV head h.
+template <int D, int COPY>
+__device__ __forceinline__ int page_chunk(const PersistLayout& lay, int pitch, int h, int t, int j) {
+  if constexpr (COPY & 4) {
+    static_assert(D == 128, "swizzled tiles hold 128-byte rows");
+    return (h * kBS + t) * D + ((j ^ (t & 7)) << 4);
+  } else {
+    return t * pitch + h * D + 16 * j;
+  }
 }
 
 // Atomic add at GPU scope with release (prior writes, and those ordered before by a barrier, are visible first)
@@ -177,10 +193,10 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
     for (int pg = 0; pg < NP; ++pg) {
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const uint8_t* row = sp[pg] + (g + 8 * r) * lay.kpitch + h * D + c * DQ;
 #pragma unroll
         for (int v = 0; v < DQ / 16; ++v) {
-          const uint4 u = *reinterpret_cast<const uint4*>(row + 16 * v);
+          const uint4 u = *reinterpret_cast<const uint4*>(
+              sp[pg] + page_chunk<D, COPY>(lay, lay.kpitch, h, g + 8 * r, c * (DQ / 16) + v));
           w[pg][r][4 * v] = u.x; w[pg][r][4 * v + 1] = u.y; w[pg][r][4 * v + 2] = u.z; w[pg][r][4 * v + 3] = u.w;
         }
       }
@@ -284,7 +300,9 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
       uint32_t vr[4][VD / 4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint8_t* row = vp + (2 * c + (j & 1) + 8 * (j >> 1)) * lay.vpitch + h * D + g * VD;
+        const int tok = 2 * c + (j & 1) + 8 * (j >> 1);
+        const uint8_t* row = (COPY & 4) ? vp + page_chunk<D, COPY>(lay, lay.vpitch, h, tok, g)
+                                        : vp + tok * lay.vpitch + h * D + g * VD;
         if constexpr (VD == 16) {
           const uint4 u = *reinterpret_cast<const uint4*>(row);
           vr[j][0] = u.x; vr[j][1] = u.y; vr[j][2] = u.z; vr[j][3] = u.w;
@@ -454,10 +472,15 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
   }
 }
 
+// tm_k, tm_v: the pools' tensor maps for COPY 4 (unused otherwise).
 template <int D, int REP, int KIND, int COPY, bool TR, int CONV>
-__global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persistent_kernel(const PagedArgs a) {
+__global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
+    paged_attn_persistent_kernel(const PagedArgs a, const __grid_constant__ CUtensorMap tm_k,
+                                 const __grid_constant__ CUtensorMap tm_v) {
   constexpr int KS = D / 16, DQ = D / 4, VB = D / 8;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // COPY 4: swizzled tiles need 1 KB aligned stages (the launch reserves the slack)
+  uint8_t* smem = (COPY & 4) ? smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : smem_raw;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int Hkv = a.Hkv, B = a.B, G = gridDim.x, cta = blockIdx.x;
@@ -600,15 +623,20 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1) paged_attn_persisten
         const uint8_t* ksrc = a.k_pool + (int64_t)blk * a.page_bytes;
         const uint8_t* vsrc = a.v_pool + (int64_t)blk * a.page_bytes;
         const int t = lane & 15;
-        if constexpr (COPY & 1) {
-          if (lane < 16) bulk_g2s_evict_first(base + t * lay.kpitch, ksrc + t * rowb, rowb, &full[st], policy);
+        if constexpr (COPY & 4) {
+          if (lane == 0) tma_load_4d_hint(base, &tm_k, 0, 0, 0, blk, &full[st], policy);
+          if (lane == 16) tma_load_4d_hint(base + lay.kpage, &tm_v, 0, 0, 0, blk, &full[st], policy);
         } else {
-          if (lane == 0) bulk_g2s_evict_first(base, ksrc, a.page_bytes, &full[st], policy);
-        }
-        if constexpr (COPY & 2) {
-          if (lane >= 16) bulk_g2s_evict_first(base + lay.kpage + t * lay.vpitch, vsrc + t * rowb, rowb, &full[st], policy);
-        } else {
-          if (lane == 16) bulk_g2s_evict_first(base + lay.kpage, vsrc, a.page_bytes, &full[st], policy);
+          if constexpr (COPY & 1) {
+            if (lane < 16) bulk_g2s_evict_first(base + t * lay.kpitch, ksrc + t * rowb, rowb, &full[st], policy);
+          } else {
+            if (lane == 0) bulk_g2s_evict_first(base, ksrc, a.page_bytes, &full[st], policy);
+          }
+          if constexpr (COPY & 2) {
+            if (lane >= 16) bulk_g2s_evict_first(base + lay.kpage + t * lay.vpitch, vsrc + t * rowb, rowb, &full[st], policy);
+          } else {
+            if (lane == 16) bulk_g2s_evict_first(base + lay.kpage, vsrc, a.page_bytes, &full[st], policy);
+          }
         }
         if constexpr (KIND == BPT_KV_INT8) {
           if (lane == 1)
@@ -898,16 +926,20 @@ int64_t persist_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int sms) {
   return kCounterBytesP + ((slots * Hq * 4 + 255) / 256) * 256 + ((slots * Hq * D * 4 + 255) / 256) * 256;
 }
 
-using PersistKernel = void (*)(PagedArgs);
+using PersistKernel = void (*)(PagedArgs, CUtensorMap, CUtensorMap);
 
 // The kernel for (D, REP, KIND): up to four query heads per KV head take the transposed consumers, eight the
 // head-major ones. FP8 keys and values convert on the conversion unit (CONV 0) at D 128 with two query heads per
 // KV head (the configs' shape, where that measured fastest), on the integer pipe (CONV 3) elsewhere.
+template <int D, int REP>
+constexpr int persist_copy() { return (REP <= 4 && D == 128) ? 4 : 0; }
+
 template <int D, int REP, int KIND>
 PersistKernel persist_kernel() {
   if constexpr (REP <= 4) {
-    if constexpr (KIND == BPT_KV_FP8 && !(D == 128 && REP == 2)) return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 3>;
-    return paged_attn_persistent_kernel<D, REP, KIND, 0, true, 0>;
+    constexpr int kCopy = persist_copy<D, REP>();
+    if constexpr (KIND == BPT_KV_FP8 && !(D == 128 && REP == 2)) return paged_attn_persistent_kernel<D, REP, KIND, kCopy, true, 3>;
+    return paged_attn_persistent_kernel<D, REP, KIND, kCopy, true, 0>;
   } else {
     return paged_attn_persistent_kernel<D, REP, KIND, 0, false, 0>;
   }
@@ -921,14 +953,36 @@ int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   // (the stall test needs every issued copy awaited in order: no early copies before the dependency wait)
   a.early = (flags & BPT_FLAG_PDL) && (flags & BPT_FLAG_KV_READY) && !a.stall ? 1 : 0;
   const int q_esize = a.q_dtype == BPT_DTYPE_F32 ? 4 : 2;
-  const PersistLayout lay = persist_layout<D, 0>(a.Hkv, a.Hq, q_esize, a.scale_bytes);
+  constexpr int kCopy = persist_copy<D, REP>();
+  const PersistLayout lay = persist_layout<D, kCopy>(a.Hkv, a.Hq, q_esize, a.scale_bytes);
   const int G = a.persist_ctas;
   // Everything but the stages and their two barriers: offsets, lengths, page lists, misc, the P tiles.
   const int fixed = 4 * (2 * a.B + 1) + 12 * a.max_cta_pages + 16 + 16 + a.Hkv * 32 * 4 * 4;
   // six stages of one page (32 KB for 8 KV heads at D 128) where they fit: config 2 measured 40.5, 37.3 and 37.0 us
   // per call at 4, 5 and 6
-  a.nst = max(2, min(kPersistStages, (kMaxSmemPerCta - fixed) / (lay.stage_bytes + 16)));
-  const int smem = a.nst * (lay.stage_bytes + 16) + fixed;
+  const int slack = (kCopy & 4) ? 1024 : 0;  // the swizzled tiles' 1 KB alignment
+  a.nst = max(2, min(kPersistStages, (kMaxSmemPerCta - fixed - slack) / (lay.stage_bytes + 16)));
+  const int smem = a.nst * (lay.stage_bytes + 16) + fixed + slack;
+  CUtensorMap tm_k, tm_v;
+  std::memset(&tm_k, 0, sizeof(tm_k));
+  std::memset(&tm_v, 0, sizeof(tm_v));
+  if constexpr ((kCopy & 4) != 0) {
+    // a pool [blocks][16 tokens][Hkv][D] of bytes as a 4-D tensor (D, tokens, heads, blocks): one box of a whole page
+    // lands head-major, [head][token][D] with the 128-byte swizzle
+    auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    if (!encode) return set_error(BPT_ERR_UNSUPPORTED, "paged attention: the driver has no tensor-map encoder");
+    const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(kBS), cuuint64_t(a.Hkv), cuuint64_t(a.num_blocks)};
+    const cuuint64_t strides[3] = {cuuint64_t(a.Hkv * D), cuuint64_t(D), cuuint64_t(a.page_bytes)};
+    const cuuint32_t box[4] = {cuuint32_t(D), cuuint32_t(kBS), cuuint32_t(a.Hkv), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int which = 0; which < 2; ++which) {
+      CUresult r = encode(which ? &tm_v : &tm_k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+                          const_cast<uint8_t*>(which ? a.v_pool : a.k_pool), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) return set_error(BPT_ERR_CUDA, "paged attention: pool tensor map (%d)", int(r));
+    }
+  }
   const PersistKernel kernel = persist_kernel<D, REP, KIND>();
   int st = set_max_smem(reinterpret_cast<const void*>(kernel), smem);
   if (st) return st;
@@ -942,7 +996,7 @@ int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (flags & BPT_FLAG_PDL) ? 1 : 0;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a, tm_k, tm_v);
   if (err != cudaSuccess) return set_error(BPT_ERR_CUDA, "paged attention (persistent) launch: %s", cudaGetErrorString(err));
   return BPT_OK;
 }

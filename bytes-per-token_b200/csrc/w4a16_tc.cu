@@ -447,15 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---- host ------------------------------------------------------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }();
-  return fn;
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
 }
 
 struct TcPlan {
