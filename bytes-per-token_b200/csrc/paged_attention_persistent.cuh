@@ -25,8 +25,9 @@ constexpr int kPersistMaxCtaPages = 4096;
 constexpr int kPersistStages = 6;
 // Each sequence's first page carries this many pages' worth of extra cost in the work split (the part it opens
 // costs a q copy, a partial, a ticket and shorter steps at its edges): CTA ranges cut the cost evenly, not the
-// page count, so a CTA whose range holds a sequence start gets correspondingly fewer pages.
-constexpr int kStartCost = 2;
+// page count, so a CTA whose range holds a sequence start gets correspondingly fewer pages. (Config 2 with the
+// swizzled tiles: 34.10, 33.68 and 33.89 us per call at 2, 3 and 4.)
+constexpr int kStartCost = 3;
 
 constexpr int64_t kCounterBytesP = 65536 * 4;  // the ticket counters, at the workspace's start (as paged_attend)
 
