@@ -835,6 +835,20 @@ def run_case(args) -> None:
             us = timer(call, 200) * 1e3 / 200
             gbs = nbytes / us / 1e3
             print(f"| {label} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} |", flush=True)
+    elif name == "decode-step":
+        # config 5 as the bench runs it (rank 0's batch): 3 warm-up steps after the capture, then `--launches` graph
+        # replays (a launch list of these gives each kernel's share of the step)
+        from bpt_b200.decode import Qwen3Decoder, Qwen3Dims
+
+        g = torch.Generator().manual_seed(1000)
+        lengths = torch.randint(1024, 8193, (64,), generator=g)
+        dec = Qwen3Decoder(Qwen3Dims(), lengths, device=dev, seed=0, capacity=args.launches + 8)
+        dec.capture()
+        for _ in range(3):
+            dec.step()
+        torch.cuda.synchronize()
+        us = _case_time(lambda i: dec.step(), args.launches)
+        print(f"{name}: {us / 1e3:.3f} ms per step")
     elif name.startswith("gate-up-m"):
         m = int(name.split("-m")[1])
         g = torch.Generator(device=dev).manual_seed(0)
@@ -951,7 +965,7 @@ def run_case(args) -> None:
         raise SystemExit(f"unknown case {name!r}")
 
 
-CASES = ["attention-config2", "attention-config3", "gemv-config1", "gemv-kernels", "gate-up-m16", "gate-up-m64", "gate-up-m256",
+CASES = ["attention-config2", "attention-config3", "gemv-config1", "gemv-kernels", "decode-step", "gate-up-m16", "gate-up-m64", "gate-up-m256",
          "norm-quant", "kivi-sweep", "kv-write-sweep", "norm-quant-sweep"]
 
 
