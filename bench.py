@@ -246,7 +246,10 @@ def build_inputs(device: torch.device, seed: int, attention: bool = True):
         w = torch.randn(6144, 2048, generator=g, device=device) * 0.02
         weights.append(quantize_w4a16(w, 128))
     x = torch.randn(1, 2048, generator=g, device=device).to(torch.bfloat16)
-    attn = [workloads.config2(device=device, seed=seed * 100 + i) for i in range(ATTN_BATCHES)] if attention else []
+    # every rank draws the same lengths (batch i's from seed i, as rank 0 builds them) with its own queries, table and
+    # pool, so the per-GPU work is the same at every N (weak scaling) and the slowest rank is not merely the busiest
+    attn = ([workloads.config2(device=device, seed=seed * 100 + i, lengths_seed=i) for i in range(ATTN_BATCHES)]
+            if attention else [])
     return weights, x, attn
 
 
@@ -641,11 +644,12 @@ def column_parallel_timing(args, world: int, device, timer) -> dict:
 
 
 def decode_step_timing(args, rank: int, device: torch.device, timer) -> dict:
-    """Config 5 on this rank: its own batch of 64 sequences (seeded by the rank), one graph-captured step per
-    launch; device time of `decode_steps` steps with the GPU leading as for the other regions."""
+    """Config 5 on this rank: its own batch of 64 sequences (lengths shared by the ranks, weights and pool seeded by the
+    rank), one graph-captured step per launch; device time of `decode_steps` steps with the GPU leading as for the
+    other regions."""
     from bpt_b200.decode import Qwen3Decoder, Qwen3Dims
 
-    g = torch.Generator().manual_seed(1000 + rank)
+    g = torch.Generator().manual_seed(1000)  # the same lengths on every rank (weak scaling), weights and pool by rank
     lengths = torch.randint(1024, 8193, (64,), generator=g)
     dec = Qwen3Decoder(Qwen3Dims(), lengths, device=device, seed=rank, capacity=args.decode_steps + 8)
     dec.capture()

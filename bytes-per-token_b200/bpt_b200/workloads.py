@@ -157,15 +157,19 @@ def empty_pool(kind: str, num_blocks: int, block_size: int, kv_heads: int, head_
 
 def paged_case(kind: str = "fp8", batch: int = 32, q_heads: int = 16, kv_heads: int = 8, head_dim: int = 128,
                lengths: tuple[int, int] | list[int] = (512, 4096), block_size: int = 16, num_blocks: int = 16384,
-               seed: int = 0, device="cuda", table_width: int | None = None) -> PagedCase:
+               seed: int = 0, device="cuda", table_width: int | None = None,
+               lengths_seed: int | None = None) -> PagedCase:
     """A filled paged pool, a random block table, ragged lengths and bf16 queries.
 
-    `lengths` is either an inclusive range (lo, hi) drawn uniformly per sequence or an explicit list.
+    `lengths` is either an inclusive range (lo, hi) drawn uniformly per sequence or an explicit list. A range is drawn
+    with `lengths_seed` when it is given and differs from `seed` (the same lengths for batches whose content differs,
+    e.g. one per rank of a weak-scaling run), else from the case's own generator first.
     """
     g = torch.Generator().manual_seed(seed)
+    lg = g if lengths_seed is None or lengths_seed == seed else torch.Generator().manual_seed(lengths_seed)
     if isinstance(lengths, tuple):
         lo, hi = lengths
-        lens = torch.randint(lo, hi + 1, (batch,), generator=g, dtype=torch.int64)
+        lens = torch.randint(lo, hi + 1, (batch,), generator=lg, dtype=torch.int64)
     else:
         lens = torch.tensor(lengths, dtype=torch.int64)
     table = block_table_for(lens, block_size, num_blocks, g, table_width)
@@ -179,8 +183,8 @@ def config1(device="cuda", seed: int = 0, keep_dense: bool = False) -> W4A16Case
     return w4a16_case(1, 6144, 2048, 128, seed, device, keep_dense)
 
 
-def config2(device="cuda", seed: int = 0) -> PagedCase:
-    return paged_case("fp8", 32, 16, 8, 128, (512, 4096), 16, 16384, seed, device)
+def config2(device="cuda", seed: int = 0, lengths_seed: int | None = None) -> PagedCase:
+    return paged_case("fp8", 32, 16, 8, 128, (512, 4096), 16, 16384, seed, device, lengths_seed=lengths_seed)
 
 
 def config3(device="cuda", seed: int = 0) -> PagedCase:
