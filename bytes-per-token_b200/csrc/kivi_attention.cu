@@ -44,6 +44,12 @@ __device__ __forceinline__ float qload(const void* q, int dt, int64_t i) {
   return static_cast<const float*>(q)[i];
 }
 
+// Byte k of a word, an unsigned code 0..255, as a float, exactly: the byte becomes the low mantissa byte of 2^23 + code
+// (one PRMT and one FADD at full rate, where a conversion instruction runs at the conversion unit's lower rate).
+__device__ __forceinline__ float code_f(uint32_t w, int k) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | uint32_t(k))) - 8388608.0f;
+}
+
 // Stored element e of a row as a float (its code for bits 4/8 low nibble handled by the caller).
 template <int BITS, int CDT>
 __device__ __forceinline__ float elem(const uint8_t* row, int e) {
@@ -66,7 +72,7 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
   constexpr int NACC = BITS == 4 ? 2 * EPL : EPL;
 
   __shared__ float q_s[REP][D];
-  __shared__ float qs_buf[kWarps * REP * D];  // the group's scaled queries; reused to combine the warps
+  __shared__ __align__(16) float qs_buf[kWarps * REP * D];  // the group's scaled queries; reused to combine the warps
   __shared__ float bias_s[kWarps][REP];
   __shared__ float p_s[kWarps][kGroup][REP];
   __shared__ float m_s[kWarps][REP], l_s[kWarps][REP];
@@ -178,13 +184,47 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
 #pragma unroll
           for (int j = 0; j < CB; ++j) buf[j] = krow[c * CB + j];
         }
-        if constexpr (BITS == 4) {
+        if constexpr (BITS == 4 && CB == 16) {  // byte e: dims e (low nibble) and e + D/2 (high nibble)
+          const uint32_t* wv = reinterpret_cast<const uint32_t*>(buf);
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int e0 = c * CB + 4 * k4;
+            const uint32_t lo = wv[k4] & 0x0F0F0F0Fu, hi = (wv[k4] >> 4) & 0x0F0F0F0Fu;
+            float xl[4], xh[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              xl[k] = code_f(lo, k);
+              xh[k] = code_f(hi, k);
+            }
+#pragma unroll
+            for (int r = 0; r < REP; ++r) {
+              const float4 ql = *reinterpret_cast<const float4*>(&qs_s[warp][r][e0]);
+              const float4 qh = *reinterpret_cast<const float4*>(&qs_s[warp][r][e0 + D / 2]);
+              sc[r] = fmaf(ql.x, xl[0], fmaf(ql.y, xl[1], fmaf(ql.z, xl[2], fmaf(ql.w, xl[3], sc[r]))));
+              sc[r] = fmaf(qh.x, xh[0], fmaf(qh.y, xh[1], fmaf(qh.z, xh[2], fmaf(qh.w, xh[3], sc[r]))));
+            }
+          }
+        } else if constexpr (BITS == 4) {
 #pragma unroll
           for (int j = 0; j < CB; ++j) {
             const int e = c * CB + j;
             const float lo = float(buf[j] & 0xF), hi = float(buf[j] >> 4);
 #pragma unroll
             for (int r = 0; r < REP; ++r) sc[r] += qs_s[warp][r][e] * lo + qs_s[warp][r][e + D / 2] * hi;
+          }
+        } else if constexpr (BITS == 8 && CB == 16) {
+          const uint32_t* wv = reinterpret_cast<const uint32_t*>(buf);
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int e0 = c * CB + 4 * k4;
+            float x[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[k] = code_f(wv[k4], k);
+#pragma unroll
+            for (int r = 0; r < REP; ++r) {
+              const float4 qv = *reinterpret_cast<const float4*>(&qs_s[warp][r][e0]);
+              sc[r] = fmaf(qv.x, x[0], fmaf(qv.y, x[1], fmaf(qv.z, x[2], fmaf(qv.w, x[3], sc[r]))));
+            }
           }
         } else {
           constexpr int EPC = CB / ESZ;
@@ -228,21 +268,39 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
         float pr[REP];
 #pragma unroll
         for (int r = 0; r < REP; ++r) pr[r] = p_s[warp][tt][r];
+        if constexpr ((BITS == 4 || BITS == 8) && (EPL == 2 || EPL == 4)) {
+          // the lane's EPL bytes in one load: codes as floats without the conversion unit
+          const uint32_t w = EPL == 4 ? *reinterpret_cast<const uint32_t*>(vrow + lane * EPL)
+                                      : uint32_t(*reinterpret_cast<const uint16_t*>(vrow + lane * EPL));
+          const uint32_t lo = BITS == 4 ? (w & 0x0F0F0F0Fu) : w, hi = (w >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-        for (int j = 0; j < EPL; ++j) {
-          const int e = lane * EPL + j;
-          if constexpr (BITS == 4) {
-            const uint8_t byte = vrow[e];
-            const float lo = float(byte & 0xF), hi = float(byte >> 4);
+          for (int j = 0; j < EPL; ++j) {
+            const float xl = code_f(lo, j);
 #pragma unroll
-            for (int r = 0; r < REP; ++r) {
-              acc[r][j] += pr[r] * lo;
-              acc[r][EPL + j] += pr[r] * hi;
+            for (int r = 0; r < REP; ++r) acc[r][j] = fmaf(pr[r], xl, acc[r][j]);
+            if constexpr (BITS == 4) {
+              const float xh = code_f(hi, j);
+#pragma unroll
+              for (int r = 0; r < REP; ++r) acc[r][EPL + j] = fmaf(pr[r], xh, acc[r][EPL + j]);
             }
-          } else {
-            const float x = elem<BITS, CDT>(vrow, e);
+          }
+        } else {
 #pragma unroll
-            for (int r = 0; r < REP; ++r) acc[r][j] += pr[r] * x;
+          for (int j = 0; j < EPL; ++j) {
+            const int e = lane * EPL + j;
+            if constexpr (BITS == 4) {
+              const uint8_t byte = vrow[e];
+              const float lo = float(byte & 0xF), hi = float(byte >> 4);
+#pragma unroll
+              for (int r = 0; r < REP; ++r) {
+                acc[r][j] += pr[r] * lo;
+                acc[r][EPL + j] += pr[r] * hi;
+              }
+            } else {
+              const float x = elem<BITS, CDT>(vrow, e);
+#pragma unroll
+              for (int r = 0; r < REP; ++r) acc[r][j] += pr[r] * x;
+            }
           }
         }
       }
