@@ -226,6 +226,26 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
               sc[r] = fmaf(qv.x, x[0], fmaf(qv.y, x[1], fmaf(qv.z, x[2], fmaf(qv.w, x[3], sc[r]))));
             }
           }
+        } else if constexpr (BITS == 16 && CB == 16 && CDT != BPT_DTYPE_F32) {  // eight 16-bit elements per load
+          const int e0 = c * 8;
+          float x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = elem<BITS, CDT>(buf, j);
+#pragma unroll
+          for (int r = 0; r < REP; ++r) {
+            const float4 q0 = *reinterpret_cast<const float4*>(&qs_s[warp][r][e0]);
+            const float4 q1 = *reinterpret_cast<const float4*>(&qs_s[warp][r][e0 + 4]);
+            sc[r] = fmaf(q0.x, x[0], fmaf(q0.y, x[1], fmaf(q0.z, x[2], fmaf(q0.w, x[3], sc[r]))));
+            sc[r] = fmaf(q1.x, x[4], fmaf(q1.y, x[5], fmaf(q1.z, x[6], fmaf(q1.w, x[7], sc[r]))));
+          }
+        } else if constexpr (BITS == 16 && CB == 16) {  // four fp32 elements per load
+          const int e0 = c * 4;
+          const float* xf = reinterpret_cast<const float*>(buf);
+#pragma unroll
+          for (int r = 0; r < REP; ++r) {
+            const float4 q0 = *reinterpret_cast<const float4*>(&qs_s[warp][r][e0]);
+            sc[r] = fmaf(q0.x, xf[0], fmaf(q0.y, xf[1], fmaf(q0.z, xf[2], fmaf(q0.w, xf[3], sc[r]))));
+          }
         } else {
           constexpr int EPC = CB / ESZ;
 #pragma unroll
@@ -283,6 +303,17 @@ __global__ void __launch_bounds__(kWarps * 32) kivi_attn_kernel(const KiviArgs a
 #pragma unroll
               for (int r = 0; r < REP; ++r) acc[r][EPL + j] = fmaf(pr[r], xh, acc[r][EPL + j]);
             }
+          }
+        } else if constexpr (BITS == 16 && CDT != BPT_DTYPE_F32 && EPL == 4) {  // four 16-bit elements in one load
+          const uint2 w = *reinterpret_cast<const uint2*>(vrow + lane * EPL * ESZ);
+          const uint32_t ww[2] = {w.x, w.y};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t bits16 = (j & 1) ? (ww[j >> 1] >> 16) : (ww[j >> 1] & 0xFFFFu);
+            const float x = CDT == BPT_DTYPE_BF16 ? __uint_as_float(bits16 << 16)
+                                                  : __half2float(__ushort_as_half(uint16_t(bits16)));
+#pragma unroll
+            for (int r = 0; r < REP; ++r) acc[r][j] = fmaf(pr[r], x, acc[r][j]);
           }
         } else {
 #pragma unroll
