@@ -413,26 +413,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster.sync();
     pdl_wait();
     const int t0 = kr * BN / a.ks, t1 = (kr + 1) * BN / a.ks;
-    if constexpr (FUSED) {
-      for (int i = tid; i < (t1 - t0) * (kTileRows / 2); i += kThreads) {
-        const int t = t0 + i / (kTileRows / 2), p = i % (kTileRows / 2);
-        float gs = 0.f, us = 0.f;
-        for (int q = 0; q < a.ks; ++q) {
-          const float* pr = cluster.map_shared_rank(part, q);
-          gs += pr[t * kTileRows + 2 * p];
-          us += pr[t * kTileRows + 2 * p + 1];
+    // Four consecutive rows of a token per item, every rank's partial requested before any is added (the ranks'
+    // shared-memory windows mapped once): distributed shared-memory loads are long-latency, so they go wide.
+    constexpr int kMaxKs = 8;
+    const float4* pr[kMaxKs];
+#pragma unroll
+    for (int q = 0; q < kMaxKs; ++q)
+      pr[q] = reinterpret_cast<const float4*>(cluster.map_shared_rank(part, q < a.ks ? q : 0));
+    for (int i = tid; i < (t1 - t0) * (kTileRows / 4); i += kThreads) {
+      const int t = t0 + i / (kTileRows / 4), r4 = i % (kTileRows / 4);
+      float4 w[kMaxKs];
+#pragma unroll
+      for (int q = 0; q < kMaxKs; ++q)
+        if (q < a.ks) w[q] = pr[q][t * (kTileRows / 4) + r4];
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < kMaxKs; ++q)  // the ranks in order: the sums do not depend on the timing
+        if (q < a.ks) {
+          v[0] += w[q].x;
+          v[1] += w[q].y;
+          v[2] += w[q].z;
+          v[3] += w[q].w;
         }
-        const int m = m0 + t;
-        if (m < a.M && n0 + 2 * p + 1 < a.N)
-          a.y[int64_t(m) * a.ldy + (n0 >> 1) + p] = __float2bfloat16_rn(silu(gs) * us);
-      }
-    } else {
-      for (int i = tid; i < (t1 - t0) * kTileRows; i += kThreads) {
-        const int t = t0 + i / kTileRows, rr = i % kTileRows;
-        float v = 0.f;
-        for (int q = 0; q < a.ks; ++q) v += cluster.map_shared_rank(part, q)[t * kTileRows + rr];
-        const int m = m0 + t;
-        if (m < a.M && n0 + rr < a.N) a.y[int64_t(m) * a.ldy + n0 + rr] = __float2bfloat16_rn(v);
+      const int m = m0 + t;
+      if (m >= a.M) continue;
+      const int rr = 4 * r4;  // rows rr .. rr + 3 of the tile
+      if constexpr (FUSED) {  // rows 2p, 2p + 1 are gate and up of output (n0 >> 1) + p
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          if (n0 + rr + 2 * e + 1 < a.N)
+            a.y[int64_t(m) * a.ldy + (n0 >> 1) + (rr >> 1) + e] = __float2bfloat16_rn(silu(v[2 * e]) * v[2 * e + 1]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (n0 + rr + e < a.N) a.y[int64_t(m) * a.ldy + n0 + rr + e] = __float2bfloat16_rn(v[e]);
       }
     }
     cluster.sync();  // the other slices' shared memory stays until every rank has read it
