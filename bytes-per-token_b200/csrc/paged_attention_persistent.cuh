@@ -31,8 +31,11 @@ constexpr int kStartCost = 3;
 
 constexpr int64_t kCounterBytesP = 65536 * 4;  // the ticket counters, at the workspace's start (as paged_attend)
 
+// A stage is a page of K then one of V (stage_bytes); its INT8 scales (K then V) and, when the page opens a part, the
+// sequence's q rows sit in the stage's aux slot (aux_bytes; q at q_off), the aux slots after all the stages, so the
+// stages keep the tiles' alignment without padding.
 struct PersistLayout {
-  int stage_bytes, kpitch, vpitch, kpage, vpage, q_off, q_bytes;
+  int stage_bytes, aux_bytes, kpitch, vpitch, kpage, vpage, q_off, q_bytes;
 };
 
 // COPY: how a page lands in its stage. 0: K and V pages as stored ([token][head][D], one bulk copy each); bits 0 / 1:
@@ -48,9 +51,15 @@ __host__ __device__ inline PersistLayout persist_layout(int Hkv, int Hq, int q_e
   p.kpage = (COPY & 4) ? kBS * rowb : kBS * p.kpitch;
   p.vpage = (COPY & 4) ? kBS * rowb : kBS * p.vpitch;
   p.q_bytes = Hq * D * q_esize;
-  p.q_off = p.kpage + p.vpage + 2 * scale_bytes;
-  p.stage_bytes = (COPY & 4) ? (p.q_off + p.q_bytes + 1023) & ~1023 : (p.q_off + p.q_bytes + 127) & ~127;
+  p.q_off = 2 * scale_bytes;
+  p.stage_bytes = (COPY & 4) ? (p.kpage + p.vpage + 1023) & ~1023 : (p.kpage + p.vpage + 127) & ~127;
+  p.aux_bytes = (p.q_off + p.q_bytes + 127) & ~127;
   return p;
+}
+
+// Stage st's aux slot (its INT8 scales, then q at q_off) in a ring of nst stages starting at `stages`.
+__host__ __device__ inline uint8_t* stage_aux(uint8_t* stages, const PersistLayout& lay, int nst, int st) {
+  return stages + nst * lay.stage_bytes + st * lay.aux_bytes;
 }
 
 // Byte offset in a stage's K (or V) page of token t's 16-byte chunk j (bytes 16 j .. 16 j + 15 of the head's D)
@@ -232,7 +241,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
       const bool live0 = g < hi_tok[pg], live1 = g + 8 < hi_tok[pg];
       float k0 = qscale, k1 = qscale;
       if constexpr (KIND == BPT_KV_INT8) {
-        const __half* kscl = reinterpret_cast<const __half*>(sp[pg] + lay.kpage + lay.vpage);
+        const __half* kscl = reinterpret_cast<const __half*>(stage_aux(stages, lay, nst, st[pg]));
         k0 *= live0 ? __half2float(kscl[g * Hkv + h]) : 0.f;
         k1 *= live1 ? __half2float(kscl[(g + 8) * Hkv + h]) : 0.f;
       }
@@ -274,7 +283,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
     for (int pg = 0; pg < NP; ++pg) {
       float vs0 = 1.f, vs1 = 1.f;
       if constexpr (KIND == BPT_KV_INT8) {
-        const __half* vscl = reinterpret_cast<const __half*>(sp[pg] + lay.kpage + lay.vpage + a.scale_bytes);
+        const __half* vscl = reinterpret_cast<const __half*>(stage_aux(stages, lay, nst, st[pg]) + a.scale_bytes);
         vs0 = g < hi_tok[pg] ? __half2float(vscl[g * Hkv + h]) : 0.f;
         vs1 = g + 8 < hi_tok[pg] ? __half2float(vscl[(g + 8) * Hkv + h]) : 0.f;
       }
@@ -386,7 +395,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
     if (np == 2) wait_page(k + 1, st[1], phs[1]);
 
     if (first) {  // q of this sequence as the QK B fragment: column g = head g / 2, part g % 2
-      const uint8_t* qrow = stages + st0 * lay.stage_bytes + lay.q_off +
+      const uint8_t* qrow = stage_aux(stages, lay, nst, st0) + lay.q_off +
                             (int64_t)(h * REP + (bhead < REP ? bhead : 0)) * D * q_esize;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
@@ -490,7 +499,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
   const int rowb = Hkv * D;
 
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.nst * lay.stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.nst * (lay.stage_bytes + lay.aux_bytes));
   uint64_t* empty = full + a.nst;
   int* off = reinterpret_cast<int*>(empty + a.nst);  // [B + 1] page offsets of the sequences
   int* slen = off + B + 1;                            // [B] lengths in tokens
@@ -591,7 +600,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
       pdl_wait();
       for (int k = 0; k < pre; ++k)
         if ((k == 0 || pseq[k - 1] != pseq[k]) && lane == 3)
-          bulk_g2s(stages + k * lay.stage_bytes + lay.q_off,
+          bulk_g2s(stage_aux(stages, lay, a.nst, k) + lay.q_off,
                    static_cast<const uint8_t*>(a.q) + (int64_t)pseq[k] * lay.q_bytes, lay.q_bytes, &full[k]);
     };
     int st = 0;        // stage of page k
@@ -641,15 +650,16 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
         }
         if constexpr (KIND == BPT_KV_INT8) {
           if (lane == 1)
-            bulk_g2s(base + lay.kpage + lay.vpage, reinterpret_cast<const uint8_t*>(a.k_scales) + (int64_t)blk * a.scale_bytes,
+            bulk_g2s(stage_aux(stages, lay, a.nst, st), reinterpret_cast<const uint8_t*>(a.k_scales) + (int64_t)blk * a.scale_bytes,
                      a.scale_bytes, &full[st]);
           if (lane == 2)
-            bulk_g2s(base + lay.kpage + lay.vpage + a.scale_bytes,
+            bulk_g2s(stage_aux(stages, lay, a.nst, st) + a.scale_bytes,
                      reinterpret_cast<const uint8_t*>(a.v_scales) + (int64_t)blk * a.scale_bytes, a.scale_bytes, &full[st]);
         }
       }
       if (first && lane == 3 && k >= pre)
-        bulk_g2s(base + lay.q_off, static_cast<const uint8_t*>(a.q) + (int64_t)b * lay.q_bytes, lay.q_bytes, &full[st]);
+        bulk_g2s(stage_aux(stages, lay, a.nst, st) + lay.q_off, static_cast<const uint8_t*>(a.q) + (int64_t)b * lay.q_bytes,
+                 lay.q_bytes, &full[st]);
       __syncwarp();
       if (lane == 0) misc[1] = k + 1;
     }
@@ -697,7 +707,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
     if (np == 2) wait_page(k + 1);
 
     if (first) {  // a new part: this sequence's q (copied with the part's first page), fresh softmax state
-      const uint8_t* kp0 = stages + (k % a.nst) * lay.stage_bytes;
+      const uint8_t* kp0 = stage_aux(stages, lay, a.nst, k % a.nst);
       const bool real = g < REP;
       const int hq = h * REP + (real ? g : 0);
       const uint8_t* qrow = kp0 + lay.q_off + (int64_t)hq * D * q_esize;
@@ -743,7 +753,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
       if (pg < np) {
         const int kk = k + pg;
         const uint8_t* kp = stages + (kk % a.nst) * lay.stage_bytes;
-        const __half* kscl = reinterpret_cast<const __half*>(kp + lay.kpage + lay.vpage);
+        const __half* kscl = reinterpret_cast<const __half*>(stage_aux(stages, lay, a.nst, kk % a.nst));
         usable[pg] = pblk[kk] >= 0 && pblk[kk] < a.num_blocks;
         const int hi = min(kBS, L - plp[kk] * kBS);
         float acc[2][2][4];  // [n-tile][even/odd k-steps][c-fragment]
@@ -814,7 +824,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
       if (pg < np && usable[pg]) {
         const int kk = k + pg;
         const uint8_t* vp = stages + (kk % a.nst) * lay.stage_bytes + lay.kpage;
-        const __half* vscl = reinterpret_cast<const __half*>(vp + lay.vpage + a.scale_bytes);
+        const __half* vscl = reinterpret_cast<const __half*>(stage_aux(stages, lay, a.nst, kk % a.nst) + a.scale_bytes);
         const int tok[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
         float pw[4];
 #pragma unroll
@@ -962,8 +972,8 @@ int launch_persist_t(const PagedArgs& a0, int flags, cudaStream_t stream) {
   // six stages of one page (32 KB for 8 KV heads at D 128) where they fit: config 2 measured 40.5, 37.3 and 37.0 us
   // per call at 4, 5 and 6
   const int slack = (kCopy & 4) ? 1024 : 0;  // the swizzled tiles' 1 KB alignment
-  a.nst = max(2, min(kPersistStages, (kMaxSmemPerCta - fixed - slack) / (lay.stage_bytes + 16)));
-  const int smem = a.nst * (lay.stage_bytes + 16) + fixed + slack;
+  a.nst = max(2, min(kPersistStages, (kMaxSmemPerCta - fixed - slack) / (lay.stage_bytes + lay.aux_bytes + 16)));
+  const int smem = a.nst * (lay.stage_bytes + lay.aux_bytes + 16) + fixed + slack;
   CUtensorMap tm_k, tm_v;
   std::memset(&tm_k, 0, sizeof(tm_k));
   std::memset(&tm_v, 0, sizeof(tm_v));
