@@ -38,18 +38,20 @@ struct PersistLayout {
   int stage_bytes, aux_bytes, kpitch, vpitch, kpage, vpage, q_off, q_bytes;
 };
 
-// COPY: how a page lands in its stage. 0: K and V pages as stored ([token][head][D], one bulk copy each); bits 0 / 1:
-// K / V token rows one by one to a 16-byte padded pitch; 4 (D = 128): K and V as 4-D tensor copies into head-major
-// tiles [head][token][128 bytes] with the 128-byte swizzle (16-byte chunk j of token row t at chunk j ^ (t mod 8)),
-// so the consumers' row reads meet no bank conflict with one copy per page (stages then start on 1 KB boundaries).
+// COPY: how a page lands in its stage. 0: K and V pages as stored ([token][head][D], one bulk copy each); 4 (D = 128):
+// K and V as 4-D tensor copies into head-major tiles [head][token][128 bytes] with the 128-byte swizzle (16-byte chunk
+// j of token row t at chunk j ^ (t mod 8)), so the consumers' row reads meet no bank conflict with one copy per page
+// (stages then start on 1 KB boundaries). (Row-by-row copies to a padded pitch, the split kernels' form, measured
+// much slower here: 32 small copies per page swamp the TMA engine.)
 template <int D, int COPY>
 __host__ __device__ inline PersistLayout persist_layout(int Hkv, int Hq, int q_esize, int scale_bytes) {
+  static_assert(COPY == 0 || COPY == 4, "pages as stored, or swizzled head-major tiles");
   PersistLayout p;
   const int rowb = Hkv * D;
-  p.kpitch = (COPY & 4) ? D : (COPY & 1) ? rowb + 16 : rowb;
-  p.vpitch = (COPY & 4) ? D : (COPY & 2) ? rowb + 16 : rowb;
-  p.kpage = (COPY & 4) ? kBS * rowb : kBS * p.kpitch;
-  p.vpage = (COPY & 4) ? kBS * rowb : kBS * p.vpitch;
+  p.kpitch = (COPY & 4) ? D : rowb;
+  p.vpitch = (COPY & 4) ? D : rowb;
+  p.kpage = kBS * rowb;
+  p.vpage = kBS * rowb;
   p.q_bytes = Hq * D * q_esize;
   p.q_off = 2 * scale_bytes;
   p.stage_bytes = (COPY & 4) ? (p.kpage + p.vpage + 1023) & ~1023 : (p.kpage + p.vpage + 127) & ~127;
@@ -162,7 +164,7 @@ __device__ __forceinline__ void consume_transposed(const PagedArgs& a, const Per
   constexpr bool kVAlu = KIND == BPT_KV_FP8 && (CONV & 2);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
-  const int h = warp, Hkv = a.Hkv, ncons = 32 * Hkv, cta = blockIdx.x, nst = a.nst;
+  const int h = warp, Hkv = a.Hkv, cta = blockIdx.x, nst = a.nst;
   const int q_esize = a.q_dtype == BPT_DTYPE_F32 ? 4 : 2;
   const int bhead = g >> 1, bpart = g & 1;  // the B column this lane feeds
   float* ptile = ptile_all + warp * 32 * 4;
@@ -632,21 +634,12 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
       if (ok) {
         const uint8_t* ksrc = a.k_pool + (int64_t)blk * a.page_bytes;
         const uint8_t* vsrc = a.v_pool + (int64_t)blk * a.page_bytes;
-        const int t = lane & 15;
         if constexpr (COPY & 4) {
           if (lane == 0) tma_load_4d_hint(base, &tm_k, 0, 0, 0, blk, &full[st], policy);
           if (lane == 16) tma_load_4d_hint(base + lay.kpage, &tm_v, 0, 0, 0, blk, &full[st], policy);
         } else {
-          if constexpr (COPY & 1) {
-            if (lane < 16) bulk_g2s_evict_first(base + t * lay.kpitch, ksrc + t * rowb, rowb, &full[st], policy);
-          } else {
-            if (lane == 0) bulk_g2s_evict_first(base, ksrc, a.page_bytes, &full[st], policy);
-          }
-          if constexpr (COPY & 2) {
-            if (lane >= 16) bulk_g2s_evict_first(base + lay.kpage + t * lay.vpitch, vsrc + t * rowb, rowb, &full[st], policy);
-          } else {
-            if (lane == 16) bulk_g2s_evict_first(base + lay.kpage, vsrc, a.page_bytes, &full[st], policy);
-          }
+          if (lane == 0) bulk_g2s_evict_first(base, ksrc, a.page_bytes, &full[st], policy);
+          if (lane == 16) bulk_g2s_evict_first(base + lay.kpage, vsrc, a.page_bytes, &full[st], policy);
         }
         if constexpr (KIND == BPT_KV_INT8) {
           if (lane == 1)
@@ -675,7 +668,6 @@ __global__ void __launch_bounds__(32 * (kMmaMaxHkv + 1), 1)
   // A step covers one page, or two consecutive pages of the same part (32 tokens): the two pages' QK chains and
   // PV accumulations interleave, and the softmax, barrier wait and release costs are paid once per two pages.
   const int h = warp;
-  const int ncons = 32 * Hkv;
   float qscale = a.sm_scale * kLog2e;
   if constexpr (KIND == BPT_KV_FP8) qscale *= a.k_scale;
   float vscale = 1.f;
