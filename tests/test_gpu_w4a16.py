@@ -36,13 +36,13 @@ def test_quantize_is_bit_exact(n, k, group):
         assert torch.equal(ow4.unpack_nibbles_int32(qweight.cpu(), k), codes)  # the unpacked codes, bit for bit
 
 
-def check_linear(m, n, k, group, seed=0, symmetric=False):
+def check_linear(m, n, k, group, seed=0, symmetric=False, x=None):
     """The kernel against the oracle of its arithmetic: the tcgen05 GEMM multiplies with the reference model's
     dense bf16 weight (compressed.py:56-69), the others scale exact group sums in fp32."""
     from bpt_b200.kernels.w4a16 import quantize_w4a16, w4a16_kernel, w4a16_linear
 
     w = dense(n, k, seed)
-    x = acts(m, k, seed + 1)
+    x = acts(m, k, seed + 1) if x is None else x
     qweight, scales, qzeros = quantize_w4a16(w.cuda(), group)
     if symmetric:
         qzeros = None
@@ -138,6 +138,18 @@ def test_streaming_gemv_shapes(m, n, k, group):
     # groups of 32/64/128, x staging beside one stage only at K = 6144, M = 8)
     check_linear(m, n, k, group, seed=m * 7 + n)
     check_linear(m, n, k, group, seed=m * 7 + n + 1, symmetric=True)
+
+
+@pytest.mark.parametrize("m,group", [(1, 128), (3, 64), (8, 128)])
+def test_streaming_gemv_activation_outliers(m, group):
+    # the streaming GEMV turns each (token, group) of x into integers under one power-of-two scale: a channel
+    # hundreds of times larger than the rest sets that scale, so the other inputs of its group keep fewer bits
+    k = 2048
+    x = acts(m, k, 7).float()
+    x[:, 5] = 300.0
+    x[:, 700] = -1000.0
+    x[0, 1500:1628] = 1e-3 * x[0, 1500:1628]  # a group of tiny values beside ordinary ones
+    check_linear(m, 1024, k, group, seed=m + 90, x=x.to(torch.bfloat16))
 
 
 def test_streaming_gemv_chain_under_pdl():
