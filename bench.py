@@ -46,6 +46,7 @@ WORKLOAD = ("config1 W4A16 GEMV (M=1, K=2048, N=6144, asym INT4 g128) + config2 
             "(B=32, 16 Q / 8 KV heads, D=128, lengths U[512,4096], page 16, 16384-page pool)")
 GEMV_COPIES = 40
 ATTN_BATCHES = 3
+E2E_GROUP = 6  # steps per wait of the kernels' stream on the copy stream in the end-to-end region
 CONFIG3_BATCHES = 2  # 2 x 545 MB of INT8 KV
 NQ_ROWS, NQ_D, NQ_COPIES = 16384, 2048, 3  # rms_norm_int8: 3 x 64 MB of bf16 rows rotate (above L2)
 SWEEP_LINEARS = [("q_proj", 2048, 2048), ("k_proj", 1024, 2048), ("v_proj", 1024, 2048), ("o_proj", 2048, 2048),
@@ -389,9 +390,10 @@ def report(args, world: int, gathered: list[dict], gemv_bytes: int, attn_bytes: 
         },
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": r0["h2d"],
                 "d2h_bytes_per_step": r0["d2h"], "ms_per_step": round(e_max / args.steps, 5),
-                "copies": "every step's inputs host->device and results device->host, pinned buffers, on a copy "
-                          "stream beside the kernels: step i+1's inputs cross while step i computes, step i's "
-                          "results while step i+1 computes"},
+                "copies": "every step's inputs host->device (one copy per step) and results device->host (one copy "
+                          "per step, as soon as the step is done), pinned buffers, on a copy stream beside the "
+                          f"kernels; inputs cross a group of {E2E_GROUP} steps ahead and the kernels' stream waits "
+                          "on the copy stream once per group"},
         "gpu_launches": 2 * args.steps,
         "gpu_launches_note": "the step region; the per-kernel regions launch K more of each kernel",
         "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": reasons,
@@ -421,11 +423,13 @@ def report(args, world: int, gathered: list[dict], gemv_bytes: int, attn_bytes: 
 def e2e_timing(args, device, timer, weights, x, attn, scale, split):
     """The same step through the public API with host buffers: a step's inputs (x, q, lengths, block table) sit in
     one pinned buffer and cross in one copy into one device buffer that the kernels read through views; the two
-    results (y, out) are views of one device buffer and come back in one copy. As a serving loop does, the copies run
-    on a copy stream beside the kernels: step i + 1's inputs cross while step i computes (each rotating batch has its
-    own device buffer, refilled only after the step that last read it), and step i's results come back while step
-    i + 1 computes (two output buffers, each reused only after its copy is done). Every step's two copies lie inside
-    the timed region, which the copy stream's last result closes. Returns (ms, h2d, d2h bytes)."""
+    results (y, out) are views of one device buffer and come back in one copy. As a serving loop with a prefetch queue
+    does, the copies run on a copy stream beside the kernels, a group of E2E_GROUP steps at a time: the next group's
+    inputs cross (one copy per step) while this group computes, and each step's results come back as soon as the step
+    is done. The kernels' stream waits on the copy stream once per group (the group's inputs have landed, the output
+    buffers it reuses have been read back), not between every two steps: a wait there would also cut the
+    programmatic dependent launch between one step's attention and the next step's GEMV. Every step's two copies lie
+    inside the timed region, which the copy stream's last result closes. Returns (ms, h2d, d2h bytes)."""
     from bpt_b200.kernels.kv_attention import attend
     from bpt_b200.kernels.w4a16 import w4a16_linear
 
@@ -439,10 +443,14 @@ def e2e_timing(args, device, timer, weights, x, attn, scale, split):
     def view(buf, off, like):
         return buf[off: off + like.numel() * like.element_size()].view(like.dtype).view(like.shape)
 
+    nb, grp = ATTN_BATCHES, E2E_GROUP
+    ring = 2 * grp  # device input and output buffers: a group being computed and the next one crossing
+    assert ring % nb == 0  # buffer r always holds batch r mod nb
     y = torch.empty(1, 6144, dtype=torch.bfloat16, device=device)
     out = torch.empty(32, 16, 128, dtype=torch.bfloat16, device=device)
     stage_in, pin_in, cases = [], [], []
-    for c in attn:  # each batch its own layout (block-table widths differ)
+    for r in range(ring):  # each batch its own layout (block-table widths differ)
+        c = attn[r % nb]
         ioff, in_total = layout([("x", x.numel() * 2), ("q", c.q.numel() * 2), ("lengths", c.lengths.numel() * 4),
                                  ("table", c.kv.block_table.numel() * 4)])
         dev = torch.empty(in_total, dtype=torch.uint8, device=device)
@@ -450,61 +458,61 @@ def e2e_timing(args, device, timer, weights, x, attn, scale, split):
                           view(dev, ioff["table"], c.kv.block_table))
         xv.copy_(x), qv.copy_(c.q), lv.copy_(c.lengths), tv.copy_(c.kv.block_table)
         stage_in.append(dev)
-        pin_in.append(dev.cpu().pin_memory())
+        if r < nb:
+            pin_in.append(dev.cpu().pin_memory())
         cases.append((xv, qv, lv, dataclasses.replace(c.kv, block_table=tv)))
     ooff, out_total = layout([("y", y.numel() * 2), ("out", out.numel() * 2)])
-    stage_out = [torch.empty(out_total, dtype=torch.uint8, device=device) for _ in range(2)]
+    stage_out = [torch.empty(out_total, dtype=torch.uint8, device=device) for _ in range(ring)]
     out_views = [(view(b, ooff["y"], y), view(b, ooff["out"], out)) for b in stage_out]
-    pin_out = [torch.empty(out_total, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    pin_out = [torch.empty(out_total, dtype=torch.uint8).pin_memory() for _ in range(ring)]
     # the bytes that cross per step (padding included), averaged over the rotating batches
-    h2d, d2h = round(sum(t.numel() for t in stage_in) / len(stage_in)), out_total
+    h2d, d2h = round(sum(t.numel() for t in stage_in[:nb]) / nb), out_total
 
     comp = torch.cuda.current_stream(device)
     copy = torch.cuda.Stream(device)
-    nb = ATTN_BATCHES
 
     def run(steps: int, lead_cycles: int):
-        in_ready = [torch.cuda.Event() for _ in range(nb)]
-        in_free = [None] * nb          # the compute that last read batch j's device buffer
-        out_free = [None, None]        # the copy that last emptied output buffer o
+        groups = -(-steps // grp)
+        in_ready = [None] * groups   # the group's input copies have landed
+        out_read = [None] * groups   # the group's results have been copied back
+        last_done = [None] * groups  # the group's last step's kernels are done
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if lead_cycles:
             torch.cuda._sleep(lead_cycles)  # the GPU waits while the host enqueues the steps
         start.record(comp)
         copy.wait_event(start)
 
-        def h2d_copy(i: int):
-            j = i % nb
+        def h2d_group(g: int):
             with torch.cuda.stream(copy):
-                if in_free[j] is not None:
-                    copy.wait_event(in_free[j])
-                stage_in[j].copy_(pin_in[j], non_blocking=True)
-                in_ready[j].record(copy)
+                if g >= 2:  # its buffers were last read by group g - 2
+                    copy.wait_event(last_done[g - 2])
+                for i in range(g * grp, min(steps, (g + 1) * grp)):
+                    stage_in[i % ring].copy_(pin_in[i % nb], non_blocking=True)
+                in_ready[g] = torch.cuda.Event()
+                in_ready[g].record(copy)
 
-        h2d_copy(0)
-        last = None
-        for i in range(steps):
-            if i + 1 < steps:
-                h2d_copy(i + 1)
-            j, o = i % nb, i % 2
-            xv, qv, lv, kv = cases[j]
-            qw, sc, qz = weights[i % GEMV_COPIES]
-            comp.wait_event(in_ready[j])
-            if out_free[o] is not None:
-                comp.wait_event(out_free[o])
-            y_v, out_v = out_views[o]
-            w4a16_linear(xv, qw, sc, qz, out=y_v, pdl=True)
-            attend(qv, kv, lv, scale, out=out_v, tokens=4096, split=split, pdl=True, kv_ready=True)
-            done = torch.cuda.Event()
-            done.record(comp)
-            in_free[j] = done
-            with torch.cuda.stream(copy):
-                copy.wait_event(done)
-                pin_out[o].copy_(stage_out[o], non_blocking=True)
-                last = torch.cuda.Event()
-                last.record(copy)
-            out_free[o] = last
-        comp.wait_event(last)
+        h2d_group(0)
+        for g in range(groups):
+            if g + 1 < groups:
+                h2d_group(g + 1)
+            comp.wait_event(in_ready[g])
+            if g >= 2:
+                comp.wait_event(out_read[g - 2])  # its output buffers were last filled by group g - 2
+            for i in range(g * grp, min(steps, (g + 1) * grp)):
+                xv, qv, lv, kv = cases[i % ring]
+                qw, sc, qz = weights[i % GEMV_COPIES]
+                y_v, out_v = out_views[i % ring]
+                w4a16_linear(xv, qw, sc, qz, out=y_v, pdl=True)
+                attend(qv, kv, lv, scale, out=out_v, tokens=4096, split=split, pdl=True, kv_ready=True)
+                done = torch.cuda.Event()
+                done.record(comp)
+                with torch.cuda.stream(copy):
+                    copy.wait_event(done)
+                    pin_out[i % ring].copy_(stage_out[i % ring], non_blocking=True)
+            last_done[g] = done
+            out_read[g] = torch.cuda.Event()
+            out_read[g].record(copy)
+        comp.wait_event(out_read[groups - 1])
         end.record(comp)
         return start, end
 
