@@ -91,51 +91,74 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
 
 
 // The part's partials are all in: out[b, hq] = sum_p w_p out_p / sum_p w_p, w_p = exp(lse_p - max lse), for
-// the query heads hq0 .. hq0 + nheads - 1. Each of the group's nthr threads takes one (query head, 4 dims) item at
-// a time and reads the parts in batches of eight with all loads issued before any is used, folding each batch in
-// with a running maximum.
+// the query heads hq0 .. hq0 + nheads - 1. Each of the group's nthr threads takes two (query head, 4 dims) items at
+// a time (items i and i + nthr) and reads the parts in batches of four with the loads of both items issued before
+// any is used, folding each batch in with a running maximum: a warp merging two heads of D = 128 pays one round
+// trip to L2 per batch of parts, not one per item (as many values in flight as batches of eight for one item, so
+// no more registers).
 template <int D>
 __device__ __forceinline__ void merge_parts(const PagedArgs& a, int b, int64_t s0, int nparts, int hq0, int nheads,
                                             int tid, int nthr) {
-  constexpr int kBatch = 8;
+  constexpr int kBatch = 4;
   const int items = nheads * (D / 4);
   const int64_t ostride = int64_t(a.Hq) * D;
-  for (int i = tid; i < items; i += nthr) {
-    const int hq = hq0 + i / (D / 4), d = 4 * (i % (D / 4));
-    const float* lse = a.ws_lse + s0 * a.Hq + hq;
-    const float* po = a.ws_out + (s0 * a.Hq + hq) * D + d;
-    float mx = -CUDART_INF_F, wsum = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p0 = 0; p0 < nparts; p0 += kBatch) {
-      float lv[kBatch];
-      float4 ov[kBatch];
+  for (int i0 = tid; i0 < items; i0 += 2 * nthr) {
+    int hq[2], d[2];
+    bool use[2];
+    const float* lse[2];
+    const float* po[2];
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const bool v = p0 + j < nparts;
-        lv[j] = v ? __ldcg(lse + int64_t(p0 + j) * a.Hq) : -CUDART_INF_F;
-        ov[j] = v ? __ldcg(reinterpret_cast<const float4*>(po + (p0 + j) * ostride)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      float bm = lv[0];
-#pragma unroll
-      for (int j = 1; j < kBatch; ++j) bm = fmaxf(bm, lv[j]);
-      const float nm = fmaxf(mx, bm);
-      if (nm == -CUDART_INF_F) continue;  // no tokens in any part so far
-      const float f = expf(mx - nm);
-      wsum *= f;
-      acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const float w = expf(lv[j] - nm);
-        wsum += w;
-        acc.x += w * ov[j].x; acc.y += w * ov[j].y; acc.z += w * ov[j].z; acc.w += w * ov[j].w;
-      }
-      mx = nm;
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * nthr;
+      use[u] = i < items;
+      hq[u] = hq0 + (use[u] ? i : i0) / (D / 4);
+      d[u] = 4 * ((use[u] ? i : i0) % (D / 4));
+      lse[u] = a.ws_lse + s0 * a.Hq + hq[u];
+      po[u] = a.ws_out + (s0 * a.Hq + hq[u]) * D + d[u];
     }
-    const int64_t o = ((int64_t)b * a.Hq + hq) * D + d;
-    out_store(a.out, a.out_dtype, o, wsum > 0.f ? acc.x / wsum : 0.f);
-    out_store(a.out, a.out_dtype, o + 1, wsum > 0.f ? acc.y / wsum : 0.f);
-    out_store(a.out, a.out_dtype, o + 2, wsum > 0.f ? acc.z / wsum : 0.f);
-    out_store(a.out, a.out_dtype, o + 3, wsum > 0.f ? acc.w / wsum : 0.f);
+    float mx[2] = {-CUDART_INF_F, -CUDART_INF_F}, wsum[2] = {0.f, 0.f};
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int p0 = 0; p0 < nparts; p0 += kBatch) {
+      float lv[2][kBatch];
+      float4 ov[2][kBatch];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const bool v = use[u] && p0 + j < nparts;
+          lv[u][j] = v ? __ldcg(lse[u] + int64_t(p0 + j) * a.Hq) : -CUDART_INF_F;
+          ov[u][j] = v ? __ldcg(reinterpret_cast<const float4*>(po[u] + (p0 + j) * ostride))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float bm = lv[u][0];
+#pragma unroll
+        for (int j = 1; j < kBatch; ++j) bm = fmaxf(bm, lv[u][j]);
+        const float nm = fmaxf(mx[u], bm);
+        if (nm == -CUDART_INF_F) continue;  // no tokens in any part so far
+        const float f = expf(mx[u] - nm);
+        wsum[u] *= f;
+        acc[u].x *= f; acc[u].y *= f; acc[u].z *= f; acc[u].w *= f;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const float w = expf(lv[u][j] - nm);
+          wsum[u] += w;
+          acc[u].x += w * ov[u][j].x; acc[u].y += w * ov[u][j].y; acc[u].z += w * ov[u][j].z;
+          acc[u].w += w * ov[u][j].w;
+        }
+        mx[u] = nm;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!use[u]) continue;
+      const int64_t o = ((int64_t)b * a.Hq + hq[u]) * D + d[u];
+      out_store(a.out, a.out_dtype, o, wsum[u] > 0.f ? acc[u].x / wsum[u] : 0.f);
+      out_store(a.out, a.out_dtype, o + 1, wsum[u] > 0.f ? acc[u].y / wsum[u] : 0.f);
+      out_store(a.out, a.out_dtype, o + 2, wsum[u] > 0.f ? acc[u].z / wsum[u] : 0.f);
+      out_store(a.out, a.out_dtype, o + 3, wsum[u] > 0.f ? acc[u].w / wsum[u] : 0.f);
+    }
   }
 }
 
