@@ -949,6 +949,17 @@ def run_case(args) -> None:
                 print(f"| {batch} x {t} | {bits} | {us:.2f} | {gbs:.0f} | {gbs / peak:.1%} |", flush=True)
                 del caches
                 torch.cuda.empty_cache()
+    elif name == "kv-write-bulk":
+        # the bulk paged FP8 write of the sweep (32 x 8 x 512 x 128 bf16 K and V), one input: a case for ncu
+        hkv, d, bs, batch, q = 8, 128, 16, 32, 512
+        g = torch.Generator(device=dev).manual_seed(1)
+        kv = workloads.empty_pool("fp8", batch * q // bs + batch, bs, hkv, d, dev, None)
+        k = torch.randn(batch, hkv, q, d, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(batch, hkv, q, d, generator=g, device=dev).to(torch.bfloat16)
+        slot = torch.arange(batch * q, device=dev, dtype=torch.int32).view(batch, q)
+        wb, wo = (slot // bs).contiguous(), (slot % bs).contiguous()
+        us = _case_time(lambda i: quantize_kv_paged(k, v, kv, wb, wo), args.launches)
+        print(f"{name}: {us:.1f} us per launch")
     elif name == "kv-write-sweep":
         print("| write | shape (B x Hkv x tokens x D, bf16 in) | us per call | GB/s | of HBM peak |\n|---|---|---|---|---|")
         hkv, d, bs = 8, 128, 16
@@ -1024,7 +1035,7 @@ def run_case(args) -> None:
 
 
 CASES = ["attention-config2", "attention-config3", "gemv-config1", "gemv-kernels", "decode-step", "gate-up-m16", "gate-up-m64", "gate-up-m256",
-         "norm-quant", "kivi-sweep", "kv-write-sweep", "norm-quant-sweep"]
+         "norm-quant", "kivi-sweep", "kv-write-bulk", "kv-write-sweep", "norm-quant-sweep"]
 
 
 def main() -> None:

@@ -1,6 +1,7 @@
 // The quantized KV-cache write path.
 //
-// bpt_paged_kv_write: one warp per (K or V, sequence, KV head, new token). The warp reads the head vector (one
+// bpt_paged_kv_write: rows that start on 16 bytes, with at least 4 new tokens, take paged_kv_write_vec_kernel (8 values
+// per lane, up to 8 tokens per warp); otherwise one warp per (K or V, sequence, KV head, new token). The warp reads the head vector (one
 // vector load per lane where strides allow), quantizes it (FP8: x / scale rounded to E4M3 with saturation; INT8:
 // an fp16 scale from the vector's absmax, then codes), and stores D bytes to slot (block, offset) of the pool (one
 // word per lane), plus the scale for INT8. Quotients are correctly rounded (div_by: the divisor's reciprocal and
@@ -117,6 +118,146 @@ __global__ void paged_kv_write_kernel(const void* __restrict__ k, const void* __
   }
 }
 
+// The same write for rows whose starts are 16-byte aligned (strides multiples of 8 elements, D of 64, 128 or 256):
+// a lane takes 8 consecutive values of one head vector with one 16-byte load (two for fp32), so D / 8 lanes cover
+// a token's head and a warp 32 / (D / 8) tokens per pass. A warp owns up to kWriteTokens consecutive new tokens of
+// one (K or V, sequence, KV head): all their loads and write slots are requested before any is quantized, the
+// quotients come in pairs from packed FMAs (the same correctly rounded division as div_by), INT8 codes are rounded
+// half to even by the 1.5 * 2^23 magic number after the clamp, and each lane stores its 8 codes as one word.
+constexpr int kWriteTokens = 8;
+
+template <int DT>
+__device__ __forceinline__ void eight_as_float(const uint8_t* p, float2 (&x)[4]) {
+  if constexpr (DT == BPT_DTYPE_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 16);
+    x[0] = make_float2(a.x, a.y); x[1] = make_float2(a.z, a.w); x[2] = make_float2(b.x, b.y); x[3] = make_float2(b.z, b.w);
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (DT == BPT_DTYPE_BF16) {
+        x[i] = make_float2(__uint_as_float(wv[i] << 16), __uint_as_float(wv[i] & 0xFFFF0000u));
+      } else {
+        x[i] = __half22float2(*reinterpret_cast<const __half2*>(&wv[i]));
+      }
+    }
+  }
+}
+
+// y / b for a pair, correctly rounded (div_by on two lanes): q = RN(y r) (adding -0 keeps the sign of a zero
+// product), e = y - q b exactly, RN(q + e r).
+__device__ __forceinline__ float2 div_by2(float2 y, float b, float r) {
+  const float2 q = ffma2(y, make_float2(r, r), make_float2(-0.f, -0.f));
+  const float2 e = ffma2(q, make_float2(-b, -b), y);
+  return ffma2(e, make_float2(r, r), q);
+}
+
+template <int DT, int D, int KIND>
+__global__ void __launch_bounds__(256) paged_kv_write_vec_kernel(
+    const void* __restrict__ k, const void* __restrict__ v, int64_t sb, int64_t sh, int64_t sq, int B, int Hkv, int Q,
+    const int32_t* __restrict__ wblocks, const int32_t* __restrict__ woffsets, uint8_t* __restrict__ k_pool,
+    uint8_t* __restrict__ v_pool, float k_scale, float v_scale, __half* __restrict__ k_scales,
+    __half* __restrict__ v_scales, int block_size, int64_t num_blocks) {
+  constexpr int LPT = D / 8;                 // lanes per token's head vector
+  constexpr int TPP = 32 / LPT;              // tokens per pass
+  constexpr int NP = kWriteTokens / TPP;     // passes
+  constexpr int ESZ = DT == BPT_DTYPE_F32 ? 4 : 2;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int QG = (Q + kWriteTokens - 1) / kWriteTokens;  // token groups per (sequence, head)
+  const int64_t per_tensor = (int64_t)B * Hkv * QG;
+  if (wid >= 2 * per_tensor) return;
+  pdl_wait();
+  const bool is_v = wid >= per_tensor;
+  const int64_t idx = is_v ? wid - per_tensor : wid;
+  int qg, h, b;
+  if (per_tensor < (int64_t(1) << 31)) {  // 32-bit index arithmetic (64-bit division is a long sequence)
+    const uint32_t i32 = uint32_t(idx), qh = uint32_t(QG) * uint32_t(Hkv);
+    b = int(i32 / qh);
+    const uint32_t rest = i32 - uint32_t(b) * qh;
+    h = int(rest / uint32_t(QG));
+    qg = int(rest - uint32_t(h) * uint32_t(QG));
+  } else {
+    qg = int(idx % QG);
+    h = int((idx / QG) % Hkv);
+    b = int(idx / ((int64_t)QG * Hkv));
+  }
+  const int q0 = qg * kWriteTokens;
+  const int nq = min(kWriteTokens, Q - q0);
+  const int sub = lane / LPT, li = lane % LPT;
+  int32_t my_blk = 0, my_off = 0;  // lane t < nq: token q0 + t's write slot
+  if (lane < nq) {
+    my_blk = wblocks[(int64_t)b * Q + q0 + lane];
+    my_off = woffsets[(int64_t)b * Q + q0 + lane];
+  }
+  const uint8_t* src = static_cast<const uint8_t*>(is_v ? v : k) +
+                       ((int64_t)b * sb + (int64_t)h * sh + (int64_t)q0 * sq + li * 8) * ESZ;
+  float2 x[NP][4];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    const int t = p * TPP + sub;
+    if (t < nq) {
+      eight_as_float<DT>(src + (int64_t)t * sq * ESZ, x[p]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[p][i] = make_float2(0.f, 0.f);
+    }
+  }
+  uint8_t* pool = is_v ? v_pool : k_pool;
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    const int t = p * TPP + sub;
+    const int32_t blk = __shfl_sync(0xffffffffu, my_blk, t < nq ? t : 0);
+    const int32_t off = __shfl_sync(0xffffffffu, my_off, t < nq ? t : 0);
+    const bool bad = blk < 0 || blk >= num_blocks || off < 0 || off >= block_size;
+    const int64_t slot = ((int64_t)blk * block_size + off) * Hkv + h;
+    uint2 word;
+    if constexpr (KIND == BPT_KV_FP8) {
+      const float s = is_v ? v_scale : k_scale;
+      const float rs = __frcp_rn(s);
+      uint16_t c[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 y = div_by2(x[p][i], s, rs);
+        c[i] = float2_to_e4m3x2(y.x, y.y);
+      }
+      word = make_uint2(uint32_t(c[0]) | (uint32_t(c[1]) << 16), uint32_t(c[2]) | (uint32_t(c[3]) << 16));
+    } else {
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fmaxf(fabsf(x[p][i].x), fabsf(x[p][i].y)));
+#pragma unroll
+      for (int o = LPT / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
+      if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
+      const float s = __half2float(s16);
+      const float rs = __frcp_rn(s);
+      uint32_t t4[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 y = div_by2(x[p][i], s, rs);
+        y.x = fminf(fmaxf(y.x, -128.f), 127.f);
+        y.y = fminf(fmaxf(y.y, -128.f), 127.f);
+        // y + 1.5 * 2^23 rounds y to an integer half to even; its low byte is the code (two's complement)
+        const float2 m = ffma2(y, make_float2(1.f, 1.f), make_float2(12582912.f, 12582912.f));
+        t4[2 * i] = __float_as_uint(m.x);
+        t4[2 * i + 1] = __float_as_uint(m.y);
+      }
+      word = make_uint2(__byte_perm(__byte_perm(t4[0], t4[1], 0x0040), __byte_perm(t4[2], t4[3], 0x0040), 0x5410),
+                        __byte_perm(__byte_perm(t4[4], t4[5], 0x0040), __byte_perm(t4[6], t4[7], 0x0040), 0x5410));
+      if (li == 0 && t < nq && !bad) (is_v ? v_scales : k_scales)[slot] = s16;
+    }
+    if (t < nq) {
+      if (bad) {
+        if (li == 0) record_error(blk < 0 || blk >= num_blocks ? kDevErrBlockIndex : kDevErrSlotIndex);
+      } else {
+        *reinterpret_cast<uint2*>(pool + slot * D + li * 8) = word;
+      }
+    }
+  }
+}
+
 template <int DT>
 int paged_write_dt(const void* k, const void* v, int64_t sb, int64_t sh, int64_t sq, int64_t B, int64_t Hkv,
                    int64_t Q, int64_t D, const int32_t* wb, const int32_t* wo, void* kp, void* vp, int kind, float ks,
@@ -131,6 +272,28 @@ int paged_write_dt(const void* k, const void* v, int64_t sb, int64_t sh, int64_t
   auto al = [](const void* p, int64_t n) { return (reinterpret_cast<uintptr_t>(p) % uintptr_t(n)) == 0; };
   const bool vec = sb % vpl == 0 && sh % vpl == 0 && sq % vpl == 0 && al(k, vbytes) && al(v, vbytes) &&
                    al(kp, vpl) && al(vp, vpl);
+  // rows that start on 16 bytes and at least 4 new tokens per sequence: eight values per lane, up to kWriteTokens
+  // tokens per warp (one or two tokens, as in a decode step, keep one warp per token: measured faster there)
+  if (Q >= 4 && (D == 64 || D == 128 || D == 256) && sb % 8 == 0 && sh % 8 == 0 && sq % 8 == 0 && al(k, 16) && al(v, 16) &&
+      al(kp, 8) && al(vp, 8)) {
+    const int64_t vwarps = 2 * B * Hkv * ((Q + kWriteTokens - 1) / kWriteTokens);
+    const int64_t vblocks = (vwarps * 32 + threads - 1) / threads;
+#define BPT_KVW8(DD, KIND)                                                                                         \
+  paged_kv_write_vec_kernel<DT, DD, KIND><<<unsigned(vblocks), threads, 0, stream>>>(                              \
+      k, v, sb, sh, sq, int(B), int(Hkv), int(Q), wb, wo, static_cast<uint8_t*>(kp), static_cast<uint8_t*>(vp), ks,  \
+      vs, static_cast<__half*>(kss), static_cast<__half*>(vss), int(bs), nb)
+    if (kind == BPT_KV_FP8) {
+      if (D == 64) BPT_KVW8(64, BPT_KV_FP8);
+      else if (D == 128) BPT_KVW8(128, BPT_KV_FP8);
+      else BPT_KVW8(256, BPT_KV_FP8);
+    } else {
+      if (D == 64) BPT_KVW8(64, BPT_KV_INT8);
+      else if (D == 128) BPT_KVW8(128, BPT_KV_INT8);
+      else BPT_KVW8(256, BPT_KV_INT8);
+    }
+#undef BPT_KVW8
+    return check_launch("paged kv write");
+  }
 #define BPT_KVW(VPL, KIND)                                                                                        \
   if (vec)                                                                                                        \
     paged_kv_write_kernel<DT, VPL, KIND, true><<<unsigned(blocks), threads, 0, stream>>>(                         \

@@ -209,6 +209,64 @@ def test_paged_write_is_bit_exact(kind, dtype, d):
         assert torch.equal(kv.k_scale.cpu(), want.k_scale) and torch.equal(kv.v_scale.cpu(), want.v_scale)
 
 
+@pytest.mark.parametrize("kind", ["fp8", "int8"])
+@pytest.mark.parametrize("q,d", [(1, 128), (4, 64), (19, 128), (9, 256)])
+def test_paged_write_many_tokens_is_bit_exact(kind, q, d):
+    # from 4 new tokens on, a warp writes up to 8 consecutive tokens of one head (19: groups of 8, 8 and 3), each to
+    # its own scattered slot, eight values per lane; a decode step's single token keeps one warp per token
+    from bpt_b200 import workloads
+    from bpt_b200.kernels.kv_write import quantize_kv_paged
+
+    b, hkv, bs, nb = 3, 8, 16, 12
+    g = torch.Generator().manual_seed(5)
+    table = torch.randperm(nb, generator=g)[: b * 2].reshape(b, 2).to(torch.int32)
+    kv = workloads.empty_pool(kind, nb, bs, hkv, d, "cuda", table.cuda(), scale=0.05)
+    k = (torch.randn(b, hkv, q, d, generator=g) * 3).to(torch.bfloat16)
+    v = (torch.randn(b, hkv, q, d, generator=g) * 3).to(torch.bfloat16)
+    pos = torch.stack([torch.randperm(2 * bs, generator=g)[:q] for _ in range(b)])
+    blocks = torch.gather(table.long(), 1, pos // bs)
+    offsets = pos % bs
+    quantize_kv_paged(k.cuda(), v.cuda(), kv, blocks.cuda(), offsets.cuda())
+    want = to_oracle(workloads.empty_pool(kind, nb, bs, hkv, d, "cuda", table.cuda(), scale=0.05))
+    okv.paged_write(want, k, v, blocks, offsets)
+    assert torch.equal(kv.k_pool.cpu(), want.k_pool) and torch.equal(kv.v_pool.cpu(), want.v_pool)
+    if kind == "int8":
+        assert torch.equal(kv.k_scale.cpu(), want.k_scale) and torch.equal(kv.v_scale.cpu(), want.v_scale)
+
+
+@pytest.mark.parametrize("q", [2, 12])
+def test_paged_write_out_of_range_slot_is_recorded_and_skipped(q):
+    # one token's write block lies outside the pool and another's offset outside its block: both are recorded on the
+    # device and written nowhere, every other token is written as usual (one warp per token at 2 tokens, warps of 8
+    # tokens at 12)
+    from bpt_b200 import _lib, workloads
+    from bpt_b200.kernels.kv_write import quantize_kv_paged
+
+    b, hkv, d, bs, nb = 2, 8, 128, 16, 8
+    table = torch.arange(4, dtype=torch.int32).reshape(b, 2)
+    kv = workloads.empty_pool("int8", nb, bs, hkv, d, "cuda", table.cuda())
+    g = torch.Generator().manual_seed(q)
+    k = torch.randn(b, hkv, q, d, generator=g).to(torch.bfloat16)
+    pos = torch.arange(q).expand(b, q)
+    blocks = torch.gather(table.long(), 1, pos // bs).clone()
+    offsets = (pos % bs).clone()
+    blocks[0, 1] = nb + 3
+    offsets[1, q - 1] = bs
+    _lib.device_error()  # clear
+    quantize_kv_paged(k.cuda(), k.cuda(), kv, blocks.cuda(), offsets.cuda())
+    assert _lib.device_error() in (2, 3)
+    keep = torch.ones(b, q, dtype=torch.bool)
+    keep[0, 1] = keep[1, q - 1] = False
+    want = to_oracle(workloads.empty_pool("int8", nb, bs, hkv, d, "cuda", table.cuda()))
+    okv.paged_write(want, k[:, :, :1], k[:, :, :1], blocks[:, :1], offsets[:, :1])  # tokens 0 of both sequences
+    for j in range(1, q):
+        rows = [i for i in range(b) if keep[i, j]]
+        if rows:
+            okv.paged_write(want, k[rows][:, :, j:j + 1], k[rows][:, :, j:j + 1], blocks[rows][:, j:j + 1],
+                            offsets[rows][:, j:j + 1])
+    assert torch.equal(kv.k_pool.cpu(), want.k_pool) and torch.equal(kv.k_scale.cpu(), want.k_scale)
+
+
 def test_paged_write_from_a_transposed_view():
     from bpt_b200 import workloads
     from bpt_b200.kernels.kv_write import quantize_kv_paged
