@@ -7,9 +7,11 @@
 // word per lane), plus the scale for INT8. Quotients are correctly rounded (div_by: the divisor's reciprocal and
 // one remainder correction) and rounding is half-to-even, so the codes equal the CPU reference's bit for bit.
 //
-// bpt_kivi_quantize: the KIVI grids of kernels/reference.py for whole key groups. Keys: one thread per
-// (sequence, head, group, channel [pair]) over the group's tokens; values: one warp per token over its
-// head vector. 4-bit codes are packed channel d low / d + D/2 high.
+// bpt_kivi_quantize: the KIVI grids of kernels/reference.py for whole key groups. At D = 128 with groups of 32 and
+// 16-bit inputs: keys one warp per (sequence, head, group), 4 channels per lane over all 32 rows at once; values one
+// warp per 8 tokens, 8 channels per lane. Otherwise keys one thread per (sequence, head, group, channel [pair]) over
+// the group's tokens and values one warp per token over its head vector. 4-bit codes are packed channel d low /
+// d + D/2 high.
 #include "common.cuh"
 
 namespace bpt {
@@ -428,10 +430,182 @@ __global__ void kivi_values_kernel(const void* __restrict__ v, int B, int Hkv, i
   }
 }
 
+// Fast paths for the configs' shape (D = 128, groups of 32 tokens, 16-bit inputs, aligned buffers), with the same
+// grid and code arithmetic as the kernels above (so the same bits).
+template <int DT>
+__device__ __forceinline__ float half16_to_float(uint32_t w, int hi) {
+  if constexpr (DT == BPT_DTYPE_BF16) return __uint_as_float(hi ? (w & 0xFFFF0000u) : (w << 16));
+  return __half2float(__ushort_as_half(uint16_t(hi ? (w >> 16) : (w & 0xFFFFu))));
+}
+
+// code = clamp(rint(x / s) + z, 0, qmax) with the correctly rounded quotient
+__device__ __forceinline__ uint32_t kivi_code(float x, float s, float rs, float z, float qmax) {
+  return uint32_t(fminf(fmaxf(rintf(div_by(x, s, rs)) + z, 0.f), qmax));
+}
+
+// Keys: one warp per (sequence, head, group of 32 tokens); lane l owns channels 4l .. 4l + 3, reads its 8 bytes of
+// all 32 rows at once (one pass over the input), and writes each token's codes as one word. 4-bit codes pack
+// channel d (low nibble) with d + 64 (high), whose codes lane l + 16 holds.
+template <int DT, int BITS>
+__global__ void __launch_bounds__(128) kivi_keys128_kernel(const void* __restrict__ k, int B, int Hkv, int T,
+                                                           uint8_t* __restrict__ codes, __half* __restrict__ kscale,
+                                                           __half* __restrict__ kzero, int64_t t_max, int64_t n_groups,
+                                                           int64_t t0) {
+  constexpr int D = 128, G = 32;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ng = T / G;
+  if (wid >= (int64_t)B * Hkv * ng) return;  // whole warps
+  const int64_t bh = wid / ng;
+  const int gi = int(wid - bh * ng);
+  const uint8_t* src = static_cast<const uint8_t*>(k) + ((bh * T + (int64_t)gi * G) * D + 4 * lane) * 2;
+  uint2 raw[G];
+#pragma unroll
+  for (int t = 0; t < G; ++t) raw[t] = *reinterpret_cast<const uint2*>(src + (int64_t)t * D * 2);
+  float lo[4] = {0.f, 0.f, 0.f, 0.f}, hi[4] = {0.f, 0.f, 0.f, 0.f};  // the range always includes 0
+#pragma unroll
+  for (int t = 0; t < G; ++t)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x = half16_to_float<DT>(j < 2 ? raw[t].x : raw[t].y, j & 1);
+      lo[j] = fminf(lo[j], x);
+      hi[j] = fmaxf(hi[j], x);
+    }
+  constexpr float qmax = float((1 << BITS) - 1);
+  float s[4], rs[4], z[4];
+  __half s16[4], z16[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    s16[j] = __float2half_rn(__fdiv_rn(hi[j] - lo[j], qmax));
+    if (!(__half2float(s16[j]) > 0.f)) s16[j] = __float2half_rn(1.0f);
+    s[j] = __half2float(s16[j]);
+    rs[j] = __frcp_rn(s[j]);
+    z[j] = fminf(fmaxf(rintf(div_by(-lo[j], s[j], rs[j])), 0.f), qmax);
+    z16[j] = __float2half_rn(z[j]);
+  }
+  const int64_t g_out = (bh * n_groups + t0 / G + gi) * D + 4 * lane;
+  *reinterpret_cast<uint2*>(kscale + g_out) =
+      make_uint2(uint32_t(__half_as_ushort(s16[0])) | (uint32_t(__half_as_ushort(s16[1])) << 16),
+                 uint32_t(__half_as_ushort(s16[2])) | (uint32_t(__half_as_ushort(s16[3])) << 16));
+  *reinterpret_cast<uint2*>(kzero + g_out) =
+      make_uint2(uint32_t(__half_as_ushort(z16[0])) | (uint32_t(__half_as_ushort(z16[1])) << 16),
+                 uint32_t(__half_as_ushort(z16[2])) | (uint32_t(__half_as_ushort(z16[3])) << 16));
+  constexpr int row_bytes = BITS == 4 ? D / 2 : D;
+  uint8_t* dst = codes + (bh * t_max + t0 + (int64_t)gi * G) * row_bytes + 4 * lane;
+#pragma unroll
+  for (int t = 0; t < G; ++t) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      word |= kivi_code(half16_to_float<DT>(j < 2 ? raw[t].x : raw[t].y, j & 1), s[j], rs[j], z[j], qmax) << (8 * j);
+    if constexpr (BITS == 4) {
+      const uint32_t up = __shfl_down_sync(0xffffffffu, word, 16);  // channels 4l + 64 .. 4l + 67
+      if (lane < 16) *reinterpret_cast<uint32_t*>(dst + (int64_t)t * row_bytes) = word | (up << 4);
+    } else {
+      *reinterpret_cast<uint32_t*>(dst + (int64_t)t * row_bytes) = word;
+    }
+  }
+}
+
+// Values: one warp per 8 consecutive tokens of a (sequence, head), 16 lanes per token with 8 channels each (one
+// 16-byte load), two tokens per pass; min and max over the token's lanes by shuffles. 4-bit codes pack channel d
+// (low nibble) with d + 64, held by lane li + 8 of the token's 16.
+template <int DT, int BITS>
+__global__ void __launch_bounds__(256) kivi_values128_kernel(const void* __restrict__ v, int B, int Hkv, int T,
+                                                             uint8_t* __restrict__ codes, __half* __restrict__ vscale,
+                                                             __half* __restrict__ vzero, int64_t t_max, int64_t t0) {
+  constexpr int D = 128, TW = 8, NP = TW / 2;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tg = (T + TW - 1) / TW;
+  if (wid >= (int64_t)B * Hkv * tg) return;  // whole warps
+  const int64_t bh = wid / tg;
+  const int tb = int(wid - bh * tg) * TW;
+  const int nt = min(TW, T - tb);
+  const int sub = lane >> 4, li = lane & 15;
+  const uint8_t* src = static_cast<const uint8_t*>(v) + ((bh * T + tb) * D + 8 * li) * 2;
+  uint4 raw[NP];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    const int t = 2 * p + sub;
+    raw[p] = t < nt ? *reinterpret_cast<const uint4*>(src + (int64_t)t * D * 2) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  constexpr float qmax = float((1 << BITS) - 1);
+  constexpr int row_bytes = BITS == 4 ? D / 2 : D;
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    const int t = 2 * p + sub;
+    const uint32_t wv[4] = {raw[p].x, raw[p].y, raw[p].z, raw[p].w};
+    float x[8];
+    float lo = 0.f, hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = half16_to_float<DT>(wv[j >> 1], j & 1);
+      lo = fminf(lo, x[j]);
+      hi = fmaxf(hi, x[j]);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    __half s16 = __float2half_rn(__fdiv_rn(hi - lo, qmax));
+    if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
+    const float s = __half2float(s16);
+    const float rs = __frcp_rn(s);
+    const float z = fminf(fmaxf(rintf(div_by(-lo, s, rs)), 0.f), qmax);
+    uint32_t w0 = 0, w1 = 0;  // channels 8 li .. 8 li + 3 and + 4 .. + 7
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      w0 |= kivi_code(x[j], s, rs, z, qmax) << (8 * j);
+      w1 |= kivi_code(x[4 + j], s, rs, z, qmax) << (8 * j);
+    }
+    const int64_t row = bh * t_max + t0 + tb + t;
+    if constexpr (BITS == 4) {
+      const uint32_t u0 = __shfl_down_sync(0xffffffffu, w0, 8), u1 = __shfl_down_sync(0xffffffffu, w1, 8);
+      if (t < nt && li < 8) *reinterpret_cast<uint2*>(codes + row * row_bytes + 8 * li) = make_uint2(w0 | (u0 << 4), w1 | (u1 << 4));
+    } else {
+      if (t < nt) *reinterpret_cast<uint2*>(codes + row * row_bytes + 8 * li) = make_uint2(w0, w1);
+    }
+    if (t < nt && li == 0) {
+      vscale[row] = s16;
+      vzero[row] = __float2half_rn(z);
+    }
+  }
+}
+
 template <int DT>
 int kivi_quantize_dt(const void* k, const void* v, int64_t B, int64_t Hkv, int64_t T, int64_t D, int bits,
                      int64_t group, void* kc, void* vc, void* ks, void* kz, void* vs, void* vz, int64_t t_max,
                      int64_t n_groups, int64_t t0, cudaStream_t stream) {
+  auto al = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+  if (DT != BPT_DTYPE_F32 && D == 128 && group == 32 && al(k, 16) && al(v, 16) && al(kc, 4) && al(vc, 8) &&
+      al(ks, 8) && al(kz, 8)) {
+    const int64_t kwarps = B * Hkv * (T / 32), vwarps = B * Hkv * ((T + 7) / 8);
+    if constexpr (DT != BPT_DTYPE_F32) {
+      if (kwarps > 0) {
+        if (bits == 4)
+          kivi_keys128_kernel<DT, 4><<<unsigned((kwarps * 32 + 127) / 128), 128, 0, stream>>>(
+              k, int(B), int(Hkv), int(T), static_cast<uint8_t*>(kc), static_cast<__half*>(ks), static_cast<__half*>(kz),
+              t_max, n_groups, t0);
+        else
+          kivi_keys128_kernel<DT, 8><<<unsigned((kwarps * 32 + 127) / 128), 128, 0, stream>>>(
+              k, int(B), int(Hkv), int(T), static_cast<uint8_t*>(kc), static_cast<__half*>(ks), static_cast<__half*>(kz),
+              t_max, n_groups, t0);
+      }
+      if (vwarps > 0) {
+        if (bits == 4)
+          kivi_values128_kernel<DT, 4><<<unsigned((vwarps * 32 + 255) / 256), 256, 0, stream>>>(
+              v, int(B), int(Hkv), int(T), static_cast<uint8_t*>(vc), static_cast<__half*>(vs), static_cast<__half*>(vz),
+              t_max, t0);
+        else
+          kivi_values128_kernel<DT, 8><<<unsigned((vwarps * 32 + 255) / 256), 256, 0, stream>>>(
+              v, int(B), int(Hkv), int(T), static_cast<uint8_t*>(vc), static_cast<__half*>(vs), static_cast<__half*>(vz),
+              t_max, t0);
+      }
+    }
+    return check_launch("kivi quantize");
+  }
   const int per_group = bits == 4 ? int(D / 2) : int(D);
   const int64_t kthreads = B * Hkv * (T / group) * per_group;
   if (kthreads > 0)

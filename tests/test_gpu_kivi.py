@@ -100,7 +100,7 @@ def test_decode_attention_returns_the_reference_contract():
 
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("d", [16, 32, 128])
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_kivi_quantize_is_bit_exact(bits, d, dtype):
     from bpt_b200.kernels.kv_write import quantize_kv
 
