@@ -424,9 +424,9 @@ def e2e_timing(args, device, timer, weights, x, attn, scale, split):
     """The same step through the public API with host buffers: a step's inputs (x, q, lengths, block table) sit in
     one pinned buffer and cross in one copy into one device buffer that the kernels read through views; the two
     results (y, out) are views of one device buffer and come back in one copy. As a serving loop with a prefetch queue
-    does, the copies run on a copy stream beside the kernels, a group of E2E_GROUP steps at a time: the next group's
-    inputs cross (one copy per step) while this group computes, and each step's results come back as soon as the step
-    is done. The kernels' stream waits on the copy stream once per group (the group's inputs have landed, the output
+    does, the copies run on a copy stream beside the kernels, a group of E2E_GROUP steps at a time (the first group a
+    single step): the next group's inputs cross (one copy per step) while this group computes, and each step's results
+    come back as soon as the step is done. The kernels' stream waits on the copy stream once per group (the group's inputs have landed, the output
     buffers it reuses have been read back), not between every two steps: a wait there would also cut the
     programmatic dependent launch between one step's attention and the next step's GEMV. Every step's two copies lie
     inside the timed region, which the copy stream's last result closes. Returns (ms, h2d, d2h bytes)."""
@@ -472,10 +472,13 @@ def e2e_timing(args, device, timer, weights, x, attn, scale, split):
     copy = torch.cuda.Stream(device)
 
     def run(steps: int, lead_cycles: int):
-        groups = -(-steps // grp)
-        in_ready = [None] * groups   # the group's input copies have landed
-        out_read = [None] * groups   # the group's results have been copied back
-        last_done = [None] * groups  # the group's last step's kernels are done
+        # groups of steps [bounds[g], bounds[g + 1]): the first holds one step, so the kernels start after one
+        # step's inputs have crossed, not a whole group's
+        bounds = [0] + list(range(1, steps, grp)) + [steps]
+        groups = len(bounds) - 1
+        in_ready = [None] * groups  # the group's input copies have landed
+        done = [None] * steps       # step i's kernels are done (its input and output buffers are read / filled)
+        read = [None] * steps       # step i's results have been copied back
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if lead_cycles:
             torch.cuda._sleep(lead_cycles)  # the GPU waits while the host enqueues the steps
@@ -484,9 +487,10 @@ def e2e_timing(args, device, timer, weights, x, attn, scale, split):
 
         def h2d_group(g: int):
             with torch.cuda.stream(copy):
-                if g >= 2:  # its buffers were last read by group g - 2
-                    copy.wait_event(last_done[g - 2])
-                for i in range(g * grp, min(steps, (g + 1) * grp)):
+                last_user = bounds[g + 1] - 1 - ring  # the latest earlier step on one of the group's buffers
+                if last_user >= 0:
+                    copy.wait_event(done[last_user])
+                for i in range(bounds[g], bounds[g + 1]):
                     stage_in[i % ring].copy_(pin_in[i % nb], non_blocking=True)
                 in_ready[g] = torch.cuda.Event()
                 in_ready[g].record(copy)
@@ -496,23 +500,23 @@ def e2e_timing(args, device, timer, weights, x, attn, scale, split):
             if g + 1 < groups:
                 h2d_group(g + 1)
             comp.wait_event(in_ready[g])
-            if g >= 2:
-                comp.wait_event(out_read[g - 2])  # its output buffers were last filled by group g - 2
-            for i in range(g * grp, min(steps, (g + 1) * grp)):
+            last_user = bounds[g + 1] - 1 - ring  # its output buffers were last filled by steps up to this one
+            if last_user >= 0:
+                comp.wait_event(read[last_user])
+            for i in range(bounds[g], bounds[g + 1]):
                 xv, qv, lv, kv = cases[i % ring]
                 qw, sc, qz = weights[i % GEMV_COPIES]
                 y_v, out_v = out_views[i % ring]
                 w4a16_linear(xv, qw, sc, qz, out=y_v, pdl=True)
                 attend(qv, kv, lv, scale, out=out_v, tokens=4096, split=split, pdl=True, kv_ready=True)
-                done = torch.cuda.Event()
-                done.record(comp)
+                done[i] = torch.cuda.Event()
+                done[i].record(comp)
                 with torch.cuda.stream(copy):
-                    copy.wait_event(done)
+                    copy.wait_event(done[i])
                     pin_out[i % ring].copy_(stage_out[i % ring], non_blocking=True)
-            last_done[g] = done
-            out_read[g] = torch.cuda.Event()
-            out_read[g].record(copy)
-        comp.wait_event(out_read[groups - 1])
+                    read[i] = torch.cuda.Event()
+                    read[i].record(copy)
+        comp.wait_event(read[steps - 1])
         end.record(comp)
         return start, end
 
