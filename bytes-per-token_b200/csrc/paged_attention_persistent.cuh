@@ -26,8 +26,10 @@ constexpr int kPersistStages = 6;
 // Each sequence's first page carries this many pages' worth of extra cost in the work split (the part it opens
 // costs a q copy, a partial, a ticket and shorter steps at its edges): CTA ranges cut the cost evenly, not the
 // page count, so a CTA whose range holds a sequence start gets correspondingly fewer pages. (Config 2 with the
-// swizzled tiles: 34.10, 33.68 and 33.89 us per call at 2, 3 and 4.)
-constexpr int kStartCost = 3;
+// swizzled tiles: 34.10, 33.68 and 33.89 us per call at 2, 3 and 4; with the split merge's loads of both items in
+// flight together, attention alone / GEMV + attention step: 33.09 / 40.11 at 2, 32.91-33.05 / 39.77-39.97 at 3,
+// 32.84-32.94 / 39.46-39.56 at 4, 33.08 / 39.82 at 5, 33.15 / 39.58 at 6.)
+constexpr int kStartCost = 4;
 
 constexpr int64_t kCounterBytesP = 65536 * 4;  // the ticket counters, at the workspace's start (as paged_attend)
 
