@@ -88,7 +88,8 @@ __global__ void paged_kv_write_kernel(const void* __restrict__ k, const void* __
     const float rs = __frcp_rn(s);
 #pragma unroll
     for (int j = 0; j < VPL; j += 2) {
-      const uint16_t two = float2_to_e4m3x2(div_by(x[j], s, rs), div_by(x[j + 1], s, rs));
+      // the quotient carries x's sign, a zero's included (div_by alone turns -0 into +0; E4M3 keeps the sign)
+      const uint16_t two = float2_to_e4m3x2(copysignf(div_by(x[j], s, rs), x[j]), copysignf(div_by(x[j + 1], s, rs), x[j + 1]));
       bytes[j] = uint8_t(two & 0xFF);
       bytes[j + 1] = uint8_t(two >> 8);
     }
@@ -221,8 +222,8 @@ __global__ void __launch_bounds__(256) paged_kv_write_vec_kernel(
       uint16_t c[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float2 y = div_by2(x[p][i], s, rs);
-        c[i] = float2_to_e4m3x2(y.x, y.y);
+        const float2 y = div_by2(x[p][i], s, rs);  // with x's sign restored on a zero quotient (E4M3 keeps -0)
+        c[i] = float2_to_e4m3x2(copysignf(y.x, x[p][i].x), copysignf(y.y, x[p][i].y));
       }
       word = make_uint2(uint32_t(c[0]) | (uint32_t(c[1]) << 16), uint32_t(c[2]) | (uint32_t(c[3]) << 16));
     } else {
@@ -432,15 +433,58 @@ __global__ void kivi_values_kernel(const void* __restrict__ v, int B, int Hkv, i
 
 // Fast paths for the configs' shape (D = 128, groups of 32 tokens, 16-bit inputs, aligned buffers), with the same
 // grid and code arithmetic as the kernels above (so the same bits).
+// Two 16-bit values of a packed word as floats (low half first).
 template <int DT>
-__device__ __forceinline__ float half16_to_float(uint32_t w, int hi) {
-  if constexpr (DT == BPT_DTYPE_BF16) return __uint_as_float(hi ? (w & 0xFFFF0000u) : (w << 16));
-  return __half2float(__ushort_as_half(uint16_t(hi ? (w >> 16) : (w & 0xFFFFu))));
+__device__ __forceinline__ float2 pair_as_float(uint32_t w) {
+  if constexpr (DT == BPT_DTYPE_BF16) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }
 
-// code = clamp(rint(x / s) + z, 0, qmax) with the correctly rounded quotient
-__device__ __forceinline__ uint32_t kivi_code(float x, float s, float rs, float z, float qmax) {
-  return uint32_t(fminf(fmaxf(rintf(div_by(x, s, rs)) + z, 0.f), qmax));
+// Packed 16-bit minimum / maximum of two words: exact, and a NaN loses to a number, as with fminf / fmaxf.
+template <int DT>
+__device__ __forceinline__ uint32_t min16x2(uint32_t a, uint32_t b) {
+  if constexpr (DT == BPT_DTYPE_BF16) {
+    const __nv_bfloat162 r = __hmin2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  } else {
+    const __half2 r = __hmin2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+}
+template <int DT>
+__device__ __forceinline__ uint32_t max16x2(uint32_t a, uint32_t b) {
+  if constexpr (DT == BPT_DTYPE_BF16) {
+    const __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  } else {
+    const __half2 r = __hmax2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+}
+
+// y / b for a pair with a divisor per lane, correctly rounded (div_by on two lanes).
+__device__ __forceinline__ float2 div_by2v(float2 y, float2 b, float2 r) {
+  const float2 q = ffma2(y, r, make_float2(-0.f, -0.f));
+  const float2 e = ffma2(q, make_float2(-b.x, -b.y), y);
+  return ffma2(e, r, q);
+}
+
+// The codes of a pair, clamp(rint(x / s) + z, 0, qmax) with the correctly rounded quotient, as
+// rint(clamp(x / s, -z, qmax - z)) + z (the same integer: z and the bounds are integers, and a NaN quotient gives 0 in
+// both); the rounding is the 1.5 * 2^23 magic number, whose bits less those of 1.5 * 2^23 are rint(y).
+__device__ __forceinline__ void kivi_code2(float2 x, float2 s, float2 rs, float2 z, float qmax, uint32_t& c0,
+                                           uint32_t& c1) {
+  float2 y = div_by2v(x, s, rs);
+  y.x = fminf(fmaxf(y.x, -z.x), qmax - z.x);
+  y.y = fminf(fmaxf(y.y, -z.y), qmax - z.y);
+  const float2 m = ffma2(y, make_float2(1.f, 1.f), make_float2(12582912.f, 12582912.f));
+  c0 = __float_as_uint(m.x) - (0x4B400000u - uint32_t(int(z.x)));
+  c1 = __float_as_uint(m.y) - (0x4B400000u - uint32_t(int(z.y)));
+}
+
+// Four codes (each below 256) as the bytes of one word, the first lowest.
+__device__ __forceinline__ uint32_t pack4(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3) {
+  return __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
 }
 
 // Keys: one warp per (sequence, head, group of 32 tokens); lane l owns channels 4l .. 4l + 3, reads its 8 bytes of
@@ -462,15 +506,21 @@ __global__ void __launch_bounds__(128) kivi_keys128_kernel(const void* __restric
   uint2 raw[G];
 #pragma unroll
   for (int t = 0; t < G; ++t) raw[t] = *reinterpret_cast<const uint2*>(src + (int64_t)t * D * 2);
-  float lo[4] = {0.f, 0.f, 0.f, 0.f}, hi[4] = {0.f, 0.f, 0.f, 0.f};  // the range always includes 0
+  uint32_t mn[2] = {0u, 0u}, mx[2] = {0u, 0u};  // packed per channel pair; the range always includes 0
 #pragma unroll
-  for (int t = 0; t < G; ++t)
+  for (int t = 0; t < G; ++t) {
+    mn[0] = min16x2<DT>(mn[0], raw[t].x);
+    mn[1] = min16x2<DT>(mn[1], raw[t].y);
+    mx[0] = max16x2<DT>(mx[0], raw[t].x);
+    mx[1] = max16x2<DT>(mx[1], raw[t].y);
+  }
+  float lo[4], hi[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float x = half16_to_float<DT>(j < 2 ? raw[t].x : raw[t].y, j & 1);
-      lo[j] = fminf(lo[j], x);
-      hi[j] = fmaxf(hi[j], x);
-    }
+  for (int p = 0; p < 2; ++p) {
+    const float2 l = pair_as_float<DT>(mn[p]), u = pair_as_float<DT>(mx[p]);
+    lo[2 * p] = l.x; lo[2 * p + 1] = l.y;
+    hi[2 * p] = u.x; hi[2 * p + 1] = u.y;
+  }
   constexpr float qmax = float((1 << BITS) - 1);
   float s[4], rs[4], z[4];
   __half s16[4], z16[4];
@@ -494,10 +544,12 @@ __global__ void __launch_bounds__(128) kivi_keys128_kernel(const void* __restric
   uint8_t* dst = codes + (bh * t_max + t0 + (int64_t)gi * G) * row_bytes + 4 * lane;
 #pragma unroll
   for (int t = 0; t < G; ++t) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      word |= kivi_code(half16_to_float<DT>(j < 2 ? raw[t].x : raw[t].y, j & 1), s[j], rs[j], z[j], qmax) << (8 * j);
+    uint32_t c[4];
+    kivi_code2(pair_as_float<DT>(raw[t].x), make_float2(s[0], s[1]), make_float2(rs[0], rs[1]), make_float2(z[0], z[1]),
+               qmax, c[0], c[1]);
+    kivi_code2(pair_as_float<DT>(raw[t].y), make_float2(s[2], s[3]), make_float2(rs[2], rs[3]), make_float2(z[2], z[3]),
+               qmax, c[2], c[3]);
+    const uint32_t word = pack4(c[0], c[1], c[2], c[3]);
     if constexpr (BITS == 4) {
       const uint32_t up = __shfl_down_sync(0xffffffffu, word, 16);  // channels 4l + 64 .. 4l + 67
       if (lane < 16) *reinterpret_cast<uint32_t*>(dst + (int64_t)t * row_bytes) = word | (up << 4);
@@ -536,30 +588,32 @@ __global__ void __launch_bounds__(256) kivi_values128_kernel(const void* __restr
   for (int p = 0; p < NP; ++p) {
     const int t = 2 * p + sub;
     const uint32_t wv[4] = {raw[p].x, raw[p].y, raw[p].z, raw[p].w};
-    float x[8];
-    float lo = 0.f, hi = 0.f;
+    // the range: packed 16-bit minima and maxima (the range always includes 0), then (-lo, hi) as one packed word
+    // whose maximum the token's 16 lanes share
+    uint32_t mn = 0u, mx = 0u;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      x[j] = half16_to_float<DT>(wv[j >> 1], j & 1);
-      lo = fminf(lo, x[j]);
-      hi = fmaxf(hi, x[j]);
+    for (int q = 0; q < 4; ++q) {
+      mn = min16x2<DT>(mn, wv[q]);
+      mx = max16x2<DT>(mx, wv[q]);
     }
+    mn = min16x2<DT>(mn, __byte_perm(mn, 0u, 0x1032));  // both halves: the lane's minimum
+    mx = max16x2<DT>(mx, __byte_perm(mx, 0u, 0x1032));
+    uint32_t nh = __byte_perm(mn ^ 0x80008000u, mx, 0x7610);  // (-lo, hi), exact
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) {
-      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-    }
+    for (int o = 8; o > 0; o >>= 1) nh = max16x2<DT>(nh, __shfl_xor_sync(0xffffffffu, nh, o));
+    const float2 nhf = pair_as_float<DT>(nh);
+    const float lo = -nhf.x, hi = nhf.y;
     __half s16 = __float2half_rn(__fdiv_rn(hi - lo, qmax));
     if (!(__half2float(s16) > 0.f)) s16 = __float2half_rn(1.0f);
     const float s = __half2float(s16);
     const float rs = __frcp_rn(s);
     const float z = fminf(fmaxf(rintf(div_by(-lo, s, rs)), 0.f), qmax);
-    uint32_t w0 = 0, w1 = 0;  // channels 8 li .. 8 li + 3 and + 4 .. + 7
+    uint32_t c[8];  // channels 8 li .. 8 li + 7
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      w0 |= kivi_code(x[j], s, rs, z, qmax) << (8 * j);
-      w1 |= kivi_code(x[4 + j], s, rs, z, qmax) << (8 * j);
-    }
+    for (int q = 0; q < 4; ++q)
+      kivi_code2(pair_as_float<DT>(wv[q]), make_float2(s, s), make_float2(rs, rs), make_float2(z, z), qmax, c[2 * q],
+                 c[2 * q + 1]);
+    const uint32_t w0 = pack4(c[0], c[1], c[2], c[3]), w1 = pack4(c[4], c[5], c[6], c[7]);
     const int64_t row = bh * t_max + t0 + tb + t;
     if constexpr (BITS == 4) {
       const uint32_t u0 = __shfl_down_sync(0xffffffffu, w0, 8), u1 = __shfl_down_sync(0xffffffffu, w1, 8);

@@ -267,6 +267,27 @@ def test_paged_write_out_of_range_slot_is_recorded_and_skipped(q):
     assert torch.equal(kv.k_pool.cpu(), want.k_pool) and torch.equal(kv.k_scale.cpu(), want.k_scale)
 
 
+@pytest.mark.parametrize("q", [1, 12])
+def test_paged_fp8_write_keeps_the_sign_of_zero(q):
+    # x / scale of a -0 input is -0, whose E4M3 code is 0x80 (the reference's cast), not 0x00
+    from bpt_b200 import workloads
+    from bpt_b200.kernels.kv_write import quantize_kv_paged
+
+    b, hkv, d, bs, nb = 2, 8, 128, 16, 4
+    table = torch.arange(4, dtype=torch.int32).reshape(b, 2)
+    kv = workloads.empty_pool("fp8", nb, bs, hkv, d, "cuda", table.cuda(), scale=0.05)
+    k = torch.randn(b, hkv, q, d, generator=torch.Generator().manual_seed(q)).to(torch.bfloat16)
+    k[:, :, :, ::3] = -0.0
+    k[:, :, :, 1::5] = 0.0
+    pos = torch.arange(q).expand(b, q)
+    blocks, offsets = torch.gather(table.long(), 1, pos // bs), pos % bs
+    quantize_kv_paged(k.cuda(), k.cuda(), kv, blocks.cuda(), offsets.cuda())
+    want = to_oracle(workloads.empty_pool("fp8", nb, bs, hkv, d, "cuda", table.cuda(), scale=0.05))
+    okv.paged_write(want, k, k, blocks, offsets)
+    assert (want.k_pool == 0x80).any()
+    assert torch.equal(kv.k_pool.cpu(), want.k_pool) and torch.equal(kv.v_pool.cpu(), want.v_pool)
+
+
 def test_paged_write_from_a_transposed_view():
     from bpt_b200 import workloads
     from bpt_b200.kernels.kv_write import quantize_kv_paged
