@@ -491,7 +491,7 @@ __device__ __forceinline__ uint32_t pack4(uint32_t c0, uint32_t c1, uint32_t c2,
 // all 32 rows at once (one pass over the input), and writes each token's codes as one word. 4-bit codes pack
 // channel d (low nibble) with d + 64 (high), whose codes lane l + 16 holds.
 template <int DT, int BITS>
-__global__ void __launch_bounds__(128) kivi_keys128_kernel(const void* __restrict__ k, int B, int Hkv, int T,
+__global__ void __launch_bounds__(128, 4) kivi_keys128_kernel(const void* __restrict__ k, int B, int Hkv, int T,
                                                            uint8_t* __restrict__ codes, __half* __restrict__ kscale,
                                                            __half* __restrict__ kzero, int64_t t_max, int64_t n_groups,
                                                            int64_t t0) {
