@@ -93,6 +93,13 @@ def test_fp8_store_with_a_scale():
     assert torch.equal(okv.fp8_load(codes, 0.5), (x / 0.5).to(torch.float8_e4m3fn).float() * 0.5)
 
 
+def test_fp8_store_keeps_the_sign_of_zero():
+    # the reference's cast (kv/quant.py:44-45) maps x / scale of a -0 input to the E4M3 code 0x80, +0 to 0x00; the
+    # GPU writes are held to the same codes
+    codes = okv.fp8_store(torch.tensor([-0.0, 0.0, -0.0, 1e-30]).to(torch.bfloat16).float(), 0.05)
+    assert codes.tolist() == [0x80, 0x00, 0x80, 0x00]
+
+
 def test_int8_rtn_restatement_matches_reference(golden):
     g = golden["int8_token"]
     q, s = okv.int8_store_rtn(g["x"])
